@@ -1,0 +1,382 @@
+"""Benchmark of the selective-scan hot path (BASELINE config 4 at seqlen 4096).
+
+One step = selective-scan forward + backward (all 8 gradients) over one batch of
+batch 32, d_inner 3072, d_state 16, seqlen 4096, bf16 I/O, fp32
+state, z gate, D, delta_bias, softplus.  Inputs are seeded synthetic tensors with the
+config's distributions (no dataset is involved).  Every tensor is ~0.8 GB, far larger
+than the 126 MB L2, so no L2 flush is needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Under torchrun each rank runs its own batch (weak scaling; the scan has no
+cross-batch exchange, so there is no data-path collective) and the reported time is
+the max over ranks.  ``--impl reference`` times the reference's CPU path (the oracle
+restatement of ``selective_scan_ref`` + autograd, on the host cores) on a bounded
+sample of the same workload and prints the same metric.
+
+Algorithmic bytes follow the reference's I/O contract (E = b*d*l, S = b*n*l, s = 2,
+C = ceil(l/2048) chunk states as in the reference's x):
+  fwd = 5*E*s + 2*S*s + b*d*C*2n*4 + d*(n+2)*4
+  bwd = 8*E*s + 2*S*s + 2*S*4 + b*d*C*2n*4 + 2*d*(n+2)*4
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "motif-mamba_b200"))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+CFG = dict(batch=32, dim=3072, seqlen=4096, dstate=16)
+METRIC = "selective-scan HBM GB/s (fwd+bwd)"
+FALLBACK_HBM = 6650.0
+
+
+def algo_bytes(batch, dim, seqlen, dstate, s=2):
+    E, S = batch * dim * seqlen, batch * dstate * seqlen
+    C = math.ceil(seqlen / 2048)
+    fwd = 5 * E * s + 2 * S * s + batch * dim * C * 2 * dstate * 4 + dim * (dstate + 2) * 4
+    bwd = 8 * E * s + 2 * S * s + 2 * S * 4 + batch * dim * C * 2 * dstate * 4 + 2 * dim * (dstate + 2) * 4
+    return fwd, bwd
+
+
+def hbm_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM, "fallback"
+
+
+def ncu_traffic(kernel):
+    """DRAM bytes per launch of `kernel` for this workload, from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "dram_traffic.txt")
+    try:
+        for line in open(p):
+            parts = line.split()
+            if len(parts) >= 3 and parts[0] == kernel and parts[1] == "config4_l4096":
+                return int(float(parts[2]))
+    except OSError:
+        pass
+    return None
+
+
+def make_inputs(device, seed):
+    b, d, l, n = CFG["batch"], CFG["dim"], CFG["seqlen"], CFG["dstate"]
+    g = torch.Generator(device=device).manual_seed(seed)
+    bf = torch.bfloat16
+    t = dict(
+        u=torch.randn(b, d, l, device=device, generator=g).to(bf),
+        delta=torch.randn(b, d, l, device=device, generator=g).to(bf),
+        z=torch.randn(b, d, l, device=device, generator=g).to(bf),
+        B=torch.randn(b, 1, n, l, device=device, generator=g).to(bf),
+        C=torch.randn(b, 1, n, l, device=device, generator=g).to(bf),
+        A=-torch.arange(1, n + 1, device=device, dtype=torch.float32).repeat(d, 1),
+        D=1 + 0.1 * torch.randn(d, device=device, generator=g),
+        delta_bias=torch.log(torch.expm1(torch.rand(d, device=device, generator=g) * 0.099 + 1e-3)),
+    )
+    dout = torch.randn(b, d, l, device=device, generator=g).to(bf)
+    return t, dout
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling around the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            import tempfile
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or not self.path:
+            return None
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append(dict(sm=float(parts[1]), smax=float(parts[2]), power=float(parts[3]),
+                                 hw=parts[5], hwt=parts[6], swt=parts[7], swp=parts[8]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return None
+        reasons = set()
+        for r in rows:
+            for key, name in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"),
+                              ("swt", "sw_thermal_slowdown"), ("swp", "sw_power_cap")):
+                if r[key].lower().startswith("active"):
+                    reasons.add(name)
+        loaded = [r for r in rows if r["power"] > 300] or rows
+        return {"sm_mhz": statistics.median(r["sm"] for r in loaded), "sm_max_mhz": max(r["smax"] for r in rows),
+                "reasons": sorted(reasons), "samples": len(rows), "samples_under_load": len(loaded)}
+
+
+def _cpu_scan_seconds(dim_s):
+    """Seconds for the oracle restatement of selective_scan_ref (fwd + autograd bwd) on
+    batch 1 x dim_s channels x seqlen 4096 (bf16 inputs, fp32 math)."""
+    from oracle import ssm_oracle as O
+    l, n = CFG["seqlen"], CFG["dstate"]
+    g = torch.Generator().manual_seed(0)
+    inp = dict(u=torch.randn(1, dim_s, l, generator=g).bfloat16(),
+               delta=torch.randn(1, dim_s, l, generator=g).bfloat16(),
+               A=-torch.arange(1, n + 1, dtype=torch.float32).repeat(dim_s, 1),
+               B=torch.randn(1, n, l, generator=g).bfloat16(), C=torch.randn(1, n, l, generator=g).bfloat16(),
+               D=torch.ones(dim_s), z=torch.randn(1, dim_s, l, generator=g).bfloat16(),
+               delta_bias=torch.full((dim_s,), -4.0))
+    dout = torch.randn(1, dim_s, l, generator=g).bfloat16()
+    t0 = time.perf_counter()
+    O.scan_with_grads(inp, dout, True)
+    return time.perf_counter() - t0
+
+
+def _cpu_sample_dim(budget_s):
+    probe = 8
+    tp = _cpu_scan_seconds(probe)
+    return int(max(probe, min(CFG["dim"], probe * budget_s / max(tp, 1e-3))))
+
+
+def _cpu_record(dim_s, dt):
+    l, n = CFG["seqlen"], CFG["dstate"]
+    f, b = algo_bytes(1, dim_s, l, n)
+    return dict(value=(f + b) / dt / 1e9, unit="GB/s", cores=torch.get_num_threads(), kind="port",
+                sample=f"selective_scan_ref fwd + autograd bwd (oracle restatement), batch 1 x {dim_s} channels "
+                       f"x seqlen {l}, n {n}, bf16 inputs, fp32 math: {dt:.2f} s per sample "
+                       f"({dim_s * l / dt / 1e6:.3f} M elements/s); metric scaled by the algorithmic bytes of the sample")
+
+
+def cpu_baseline_sample(threads=None, budget_s=15.0):
+    if threads:
+        torch.set_num_threads(threads)
+    dim_s = _cpu_sample_dim(budget_s)
+    dt = _cpu_scan_seconds(dim_s)
+    return _cpu_record(dim_s, dt), dt
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    torch.set_num_threads(os.cpu_count() or 1)
+    dim_s = _cpu_sample_dim(max(1.0, 120.0 / (args.warmup + args.steps)))
+    times = []
+    for i in range(args.warmup + args.steps):
+        dt = _cpu_scan_seconds(dim_s)
+        if i >= args.warmup:
+            times.append(dt)
+    cb = _cpu_record(dim_s, statistics.median(times))
+    v = cb["value"]
+    fwd_b, bwd_b = algo_bytes(**CFG)
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": (fwd_b + bwd_b) / (v * 1e9) * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "config": {"workload": "selective scan fwd+bwd, BASELINE config 4 at seqlen 4096 "
+                                                        "(32 x 3072 x 4096, n 16, bf16 I/O)",
+                                            "batch": CFG["batch"], "d_inner": CFG["dim"],
+                                            "seqlen": CFG["seqlen"], "d_state": CFG["dstate"]},
+            "cpu_baseline": cb, "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0,
+                                        "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+
+    from motif_ssm import selective_scan_cuda as ssc, selective_scan_fn
+
+    t, dout = make_inputs(dev, seed=1234 + rank)
+    fwd_b, bwd_b = algo_bytes(**CFG)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(ev=None):
+        if ev is not None:
+            ev[0].record(stream)
+        out, x, out_z = ssc.fwd(t["u"], t["delta"], t["A"], t["B"], t["C"], D=t["D"], z=t["z"],
+                                delta_bias=t["delta_bias"], delta_softplus=True)
+        if ev is not None:
+            ev[1].record(stream)
+        grads = ssc.bwd(t["u"], t["delta"], t["A"], t["B"], t["C"], D=t["D"], z=t["z"], delta_bias=t["delta_bias"],
+                        dout=dout, x=x, out=out, dz=None, delta_softplus=True, recompute_out_z=False)
+        if ev is not None:
+            ev[2].record(stream)
+        return out_z, grads
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        start.record(stream)
+        for i in range(args.steps):
+            step(evs[i])
+        end.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    total_ms = start.elapsed_time(end)
+    fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    tt = torch.tensor([total_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    ms_per_step = tt.item() / args.steps
+    value = (fwd_b + bwd_b) * world / (ms_per_step * 1e-3) / 1e9
+    launches_per_step = (2 if ssc_needs_split() else 1) + 3  # fwd (+carry) ; bwd main + 2 dB/dC converts
+
+    # ---- end to end through the public API: host (pinned) inputs in, gradients out ----
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(t, dout, dev, stream, world, selective_scan_fn, fwd_b + bwd_b, max(3, args.steps // 4),
+                      dist if world > 1 else None)
+
+    peak, peak_kind = hbm_peak()
+    dom_ms, dom_bytes, dom_name = (bwd_ms, bwd_b, "ss_bwd") if bwd_ms >= fwd_ms else (fwd_ms, fwd_b, "ss_fwd")
+    achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
+    traffic = ncu_traffic(dom_name)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu, _ = cpu_baseline_sample(os.cpu_count(), budget_s=15.0)
+    if rank == 0:
+        clocks = clk.summary()
+        line = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "selective scan fwd+bwd, BASELINE config 4 at seqlen 4096 "
+                                   "(32 x 3072 x 4096 per GPU, n 16, bf16 I/O, fp32 state, z, D, delta_bias, softplus)",
+                       "batch_per_gpu": CFG["batch"], "d_inner": CFG["dim"], "seqlen": CFG["seqlen"],
+                       "d_state": CFG["dstate"], "l2": "inputs larger than L2 (0.8 GB per tensor), no flush",
+                       "algorithmic_bytes_per_step": fwd_b + bwd_b},
+            "kernels": {"ss_fwd": {"ms": fwd_ms, "GB/s": fwd_b / (fwd_ms * 1e-3) / 1e9,
+                                   "frac_of_hbm": fwd_b / (fwd_ms * 1e-3) / 1e9 / peak},
+                        "ss_bwd": {"ms": bwd_ms, "GB/s": bwd_b / (bwd_ms * 1e-3) / 1e9,
+                                   "frac_of_hbm": bwd_b / (bwd_ms * 1e-3) / 1e9 / peak}},
+            "roofline": {"bound": "hbm", "kernel": dom_name, "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
+                         if peak_kind == "measured" else "fallback 6650 GB/s", "traffic": traffic},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def ssc_needs_split():
+    import ctypes
+    from motif_ssm import _lib
+    a = _lib.SsFwdArgs()
+    a.batch, a.dim, a.seqlen, a.dstate, a.n_groups, a.itype = (CFG["batch"], CFG["dim"], CFG["seqlen"],
+                                                               CFG["dstate"], 1, _lib.MSS_BF16)
+    nb = ctypes.c_int64(0)
+    _lib.check(_lib.lib.ss_fwd_workspace_size(ctypes.byref(a), ctypes.byref(nb)))
+    return nb.value > 0
+
+
+def run_e2e(t, dout, dev, stream, world, selective_scan_fn, algo, steps, dist):
+    """selective_scan_fn (autograd) per step: pinned host inputs -> device, forward,
+    backward, all 8 gradients -> pinned host.  Timed with CUDA events, max over ranks."""
+    keys = ("u", "delta", "A", "B", "C", "D", "z", "delta_bias")
+    host = {k: t[k].cpu().pin_memory() for k in keys}
+    host_dout = dout.cpu().pin_memory()
+    dev_bufs = {k: torch.empty_like(t[k]) for k in keys}
+    dev_dout = torch.empty_like(dout)
+    host_grads = {k: torch.empty(t[k].shape, dtype=t[k].dtype).pin_memory() for k in keys}
+    h2d = sum(v.numel() * v.element_size() for v in host.values()) + host_dout.numel() * host_dout.element_size()
+    d2h = sum(v.numel() * v.element_size() for v in host_grads.values())
+
+    def one():
+        for k in keys:
+            dev_bufs[k].copy_(host[k], non_blocking=True)
+        dev_dout.copy_(host_dout, non_blocking=True)
+        leaves = {k: dev_bufs[k].detach().requires_grad_(True) for k in keys}
+        out = selective_scan_fn(leaves["u"], leaves["delta"], leaves["A"], leaves["B"], leaves["C"], leaves["D"],
+                                z=leaves["z"], delta_bias=leaves["delta_bias"], delta_softplus=True)
+        out.backward(dev_dout)
+        for k in keys:
+            host_grads[k].copy_(leaves[k].grad, non_blocking=True)
+
+    for _ in range(2):
+        one()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(steps):
+        one()
+    e.record(stream)
+    torch.cuda.synchronize()
+    tt = torch.tensor([s.elapsed_time(e)], device=dev, dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    ms = tt.item() / steps
+    return {"value": algo * world / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms, "steps": steps,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "api": "motif_ssm.selective_scan_fn forward + autograd backward, pinned host buffers"}
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,184 @@
+/*
+ * motif_ssm.h -- C ABI of the B200 (sm_100a) selective-scan hot path.
+ *
+ * Plain pointers, element strides and sizes; no framework types.  Every entry
+ * point is asynchronous on the caller's stream, allocates nothing (callers pass
+ * every output and, where one is needed, a workspace whose size a *_workspace_size
+ * query returns), never aborts, and returns an int status (MSS_OK on success).
+ * The message of the last failure on the calling thread is ss_last_error().
+ *
+ * The reference interfaces each entry point replaces (paths relative to the
+ * reference project, 4354ce38/Motif-Mamba, a fork of mamba_ssm 2.2.6.post3):
+ *
+ *   ss_fwd            selective_scan_cuda.fwd   csrc/selective_scan/selective_scan.cpp:270-413, 621-627
+ *   ss_bwd            selective_scan_cuda.bwd   csrc/selective_scan/selective_scan.cpp:415-618, 628-636
+ *   conv1d_fwd        causal_conv1d_fwd_function   (external causal-conv1d; call sites
+ *                     mamba_ssm/ops/selective_scan_interface.py:482-484, 567-569)
+ *   conv1d_bwd        causal_conv1d_bwd_function   (selective_scan_interface.py:635-637)
+ *   conv1d_update     causal_conv1d_update_function / causal_conv1d_update
+ *                     (mamba_ssm/modules/mamba_simplemotif.py:352-358)
+ *   ssm_state_update  mamba_ssm.ops.triton.selective_state_update.selective_state_update
+ *                     (mamba_ssm/modules/mamba_simplemotif.py:396-399)
+ *
+ * Layout conventions.  Sequence tensors are (batch, channels, seqlen) with the
+ * sequence dimension unit-stride; strides below are in ELEMENTS.  B and C of the
+ * scan are "variable" (batch, groups, dstate, seqlen).  A, D, delta_bias are fp32.
+ */
+#ifndef MOTIF_SSM_H
+#define MOTIF_SSM_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MSS_API __attribute__((visibility("default")))
+#else
+#define MSS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define MSS_OK 0
+#define MSS_ERR_INVALID 1       /* bad argument: shape, stride, null pointer, flag combination */
+#define MSS_ERR_UNSUPPORTED 2   /* valid for the reference but not implemented here (e.g. complex A) */
+#define MSS_ERR_ALIGNMENT 3     /* pointer alignment the kernel needs is not met */
+#define MSS_ERR_WORKSPACE 4     /* workspace missing or smaller than *_workspace_size */
+#define MSS_ERR_CUDA 5          /* a CUDA runtime call or kernel launch failed */
+
+/* element types of the sequence tensors (u, delta, z, B, C, out, ...) */
+#define MSS_F32 0
+#define MSS_F16 1
+#define MSS_BF16 2
+
+/* Length, in timesteps, of the chunks whose end states ss_fwd writes into x.
+ * x has shape (batch, dim, ceil(seqlen / ss_chunk_len()), 2 * dstate) fp32 and
+ * holds (cumulative decay, state) pairs; x[:, :, -1, 1::2] is the final state. */
+MSS_API int32_t ss_chunk_len(void);
+
+/* Largest dstate the kernels accept. */
+MSS_API int32_t ss_max_dstate(void);
+
+typedef struct {
+    int64_t batch, dim, seqlen, dstate, n_groups;
+    int32_t itype;           /* MSS_F32 / MSS_F16 / MSS_BF16 for u, delta, B, C, z, out, out_z */
+    int32_t delta_softplus;  /* 1: delta <- softplus(delta + delta_bias) (threshold 20) */
+    const void *u;      int64_t u_bs, u_ds;
+    const void *delta;  int64_t delta_bs, delta_ds;
+    const float *A;     int64_t A_ds, A_ns;            /* (dim, dstate) */
+    const void *B;      int64_t B_bs, B_gs, B_ns;      /* (batch, n_groups, dstate, seqlen) */
+    const void *C;      int64_t C_bs, C_gs, C_ns;
+    const float *D;     int64_t D_s;                   /* nullable, (dim,) */
+    const float *delta_bias; int64_t delta_bias_s;     /* nullable, (dim,) */
+    const void *z;      int64_t z_bs, z_ds;            /* nullable */
+    void *out;          int64_t out_bs, out_ds;        /* y + D*u, before the z gate */
+    void *out_z;        int64_t out_z_bs, out_z_ds;    /* required iff z: out * silu(z) */
+    float *x;           /* contiguous (batch, dim, n_chunks, 2*dstate) */
+    void *workspace;    int64_t workspace_bytes;
+} ss_fwd_args;
+
+typedef struct {
+    int64_t batch, dim, seqlen, dstate, n_groups;
+    int32_t itype;
+    int32_t delta_softplus;
+    int32_t recompute_out_z; /* 1: also write out_z = out * silu(z) (needs z) */
+    int32_t _pad0;
+    const void *u;      int64_t u_bs, u_ds;
+    const void *delta;  int64_t delta_bs, delta_ds;
+    const float *A;     int64_t A_ds, A_ns;
+    const void *B;      int64_t B_bs, B_gs, B_ns;
+    const void *C;      int64_t C_bs, C_gs, C_ns;
+    const float *D;     int64_t D_s;                   /* nullable */
+    const float *delta_bias; int64_t delta_bias_s;     /* nullable */
+    const void *z;      int64_t z_bs, z_ds;            /* nullable */
+    const void *out;    int64_t out_bs, out_ds;        /* forward's pre-gate out; required iff z */
+    const float *x;     /* ss_fwd's chunk states, contiguous (batch, dim, n_chunks, 2*dstate) */
+    const void *dout;   int64_t dout_bs, dout_ds;
+    void *du;           int64_t du_bs, du_ds;
+    void *ddelta;       int64_t ddelta_bs, ddelta_ds;
+    float *dA;          /* contiguous (dim, dstate), overwritten */
+    void *dB;           /* contiguous (batch, n_groups, dstate, seqlen), itype, overwritten */
+    void *dC;
+    float *dD;          /* nullable iff D is null, (dim,), overwritten */
+    float *ddelta_bias; /* nullable iff delta_bias is null, (dim,), overwritten */
+    void *dz;           int64_t dz_bs, dz_ds;          /* required iff z */
+    void *out_z;        int64_t out_z_bs, out_z_ds;    /* required iff recompute_out_z */
+    void *workspace;    int64_t workspace_bytes;
+} ss_bwd_args;
+
+typedef struct {
+    int64_t batch, dim, seqlen, width;
+    int32_t itype;              /* x, out (and dout, dx in the backward) */
+    int32_t wtype;              /* weight and bias element type */
+    int32_t silu;
+    int32_t _pad0;
+    const void *x;      int64_t x_bs, x_ds;
+    const void *weight; int64_t w_ds, w_ks;            /* (dim, width) */
+    const void *bias;                                  /* nullable, contiguous (dim,) */
+    void *out;          int64_t out_bs, out_ds;        /* forward output */
+    const void *dout;   int64_t dout_bs, dout_ds;      /* backward only */
+    void *dx;           int64_t dx_bs, dx_ds;          /* backward only */
+    float *dweight;     /* backward only: contiguous (dim, width) fp32, overwritten */
+    float *dbias;       /* backward only: nullable (dim,) fp32, overwritten */
+} conv1d_args;
+
+typedef struct {
+    int64_t batch, dim, width, state_len;   /* state_len >= width (reference: == width) */
+    int32_t itype;              /* x, out */
+    int32_t wtype;              /* weight, bias */
+    int32_t stype;              /* conv_state element type */
+    int32_t silu;
+    const void *x;      int64_t x_bs;                  /* (batch, dim) */
+    void *conv_state;   int64_t cs_bs, cs_ds;          /* (batch, dim, state_len), updated in place */
+    const void *weight; int64_t w_ds, w_ks;
+    const void *bias;                                  /* nullable */
+    void *out;          int64_t out_bs;                /* (batch, dim) */
+} conv1d_update_args;
+
+typedef struct {
+    int64_t batch, dim, dstate, n_groups;
+    int32_t itype;              /* x, dt, z, out, B, C */
+    int32_t stype;              /* state element type */
+    int32_t dt_softplus;
+    int32_t _pad0;
+    void *state;        int64_t st_bs, st_ds, st_ns;   /* (batch, dim, dstate), updated in place */
+    const void *x;      int64_t x_bs;                  /* (batch, dim) */
+    const void *dt;     int64_t dt_bs;
+    const float *A;     int64_t A_ds, A_ns;
+    const void *B;      int64_t B_bs, B_gs;            /* (batch, n_groups, dstate), dstate unit-stride */
+    const void *C;      int64_t C_bs, C_gs;
+    const float *D;                                    /* nullable (dim,) */
+    const void *z;      int64_t z_bs;                  /* nullable */
+    const float *dt_bias;                              /* nullable (dim,) */
+    void *out;          int64_t out_bs;
+} ssm_state_update_args;
+
+/* Workspace bytes ss_fwd / ss_bwd need for these arguments (0 means none). */
+MSS_API int ss_fwd_workspace_size(const ss_fwd_args *a, int64_t *bytes);
+MSS_API int ss_bwd_workspace_size(const ss_bwd_args *a, int64_t *bytes);
+
+/* selective scan forward: writes out, out_z (iff z) and x.  (selective_scan.cpp:270-413) */
+MSS_API int ss_fwd(const ss_fwd_args *a, void *stream);
+/* selective scan backward: writes du, ddelta, dA, dB, dC, dD, ddelta_bias, dz, out_z.  (selective_scan.cpp:415-618) */
+MSS_API int ss_bwd(const ss_bwd_args *a, void *stream);
+/* depthwise causal conv1d (+SiLU) forward / backward (causal-conv1d API) */
+MSS_API int conv1d_fwd(const conv1d_args *a, void *stream);
+MSS_API int conv1d_bwd(const conv1d_args *a, void *stream);
+/* one decode step of the conv: shifts conv_state left by one, appends x, writes out */
+MSS_API int conv1d_update(const conv1d_update_args *a, void *stream);
+/* one decode step of the SSM: updates state in place, writes out */
+MSS_API int ssm_state_update(const ssm_state_update_args *a, void *stream);
+
+/* Message of the last failure on the calling thread ("" if none). */
+MSS_API const char *ss_last_error(void);
+/* Library version string. */
+MSS_API const char *ss_version(void);
+/* sizeof() of each argument struct, for binding-side layout checks:
+ * out[0..4] = ss_fwd_args, ss_bwd_args, conv1d_args, conv1d_update_args, ssm_state_update_args */
+MSS_API void ss_abi_struct_sizes(int64_t out[5]);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MOTIF_SSM_H */

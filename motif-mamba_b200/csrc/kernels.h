@@ -1,0 +1,61 @@
+// Internal launch interface between the C-ABI layer (abi.cu) and the kernels.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "motif_ssm.h"
+
+namespace mss {
+
+struct FwdParams {
+    int batch, dim, seqlen, dstate, n_groups, dpg, tiles_per_group;
+    int softplus, n_seg, seg_len, n_chunks, aligned;
+    const void *u, *delta, *B, *C, *z;
+    void *out, *out_z;
+    int64_t u_bs, u_ds, delta_bs, delta_ds, B_bs, B_gs, B_ns, C_bs, C_gs, C_ns, z_bs, z_ds;
+    int64_t out_bs, out_ds, out_z_bs, out_z_ds;
+    const float *A;
+    int64_t A_ds, A_ns;
+    const float *D;
+    int64_t D_s;
+    const float *delta_bias;
+    int64_t delta_bias_s;
+    float *x;
+    float *ws_h, *ws_dts;  // segment carries (n_seg > 1)
+};
+
+struct BwdParams {
+    int batch, dim, seqlen, dstate, n_groups, dpg, tiles_per_group, kgroups;
+    int softplus, recompute_out_z, n_chunks, aligned;
+    int64_t lpitch;  // row pitch (floats) of the fp32 dB/dC accumulators
+    const void *u, *delta, *B, *C, *z, *out, *dout;
+    int64_t u_bs, u_ds, delta_bs, delta_ds, B_bs, B_gs, B_ns, C_bs, C_gs, C_ns, z_bs, z_ds;
+    int64_t out_bs, out_ds, dout_bs, dout_ds;
+    const float *A;
+    int64_t A_ds, A_ns;
+    const float *D;
+    int64_t D_s;
+    const float *delta_bias;
+    int64_t delta_bias_s;
+    const float *x;
+    void *du, *ddelta, *dz, *out_z;
+    int64_t du_bs, du_ds, ddelta_bs, ddelta_ds, dz_bs, dz_ds, out_z_bs, out_z_ds;
+    float *dA, *dD, *ddelta_bias;
+    float *acc_dB, *acc_dC;  // fp32 accumulators (batch, n_groups, dstate, lpitch)
+    float *ws_dh;            // reverse-recurrence carry between chunks (batch, dim, 16)
+};
+
+int fwd_state_pad(int dstate);
+int fwd_channels_per_cta(int dstate);
+cudaError_t launch_ss_fwd(const FwdParams &p, int itype, bool has_z, cudaStream_t st);
+
+constexpr int kBwdChannelsPerGroup = 16;  // channel lanes per CTA pass (256 threads / 16 states)
+cudaError_t launch_ss_bwd(const BwdParams &p, int itype, bool has_z, cudaStream_t st);
+cudaError_t launch_conv1d_fwd(const conv1d_args &a, bool vec, cudaStream_t st);
+cudaError_t launch_conv1d_bwd(const conv1d_args &a, bool vec, cudaStream_t st);
+cudaError_t launch_conv1d_update(const conv1d_update_args &a, cudaStream_t st);
+cudaError_t launch_state_update(const ssm_state_update_args &a, cudaStream_t st);
+cudaError_t launch_acc_to_out(const float *acc, int64_t lpitch, void *out, int itype, int64_t rows,
+                              int64_t seqlen, cudaStream_t st);
+
+}  // namespace mss

@@ -1,0 +1,284 @@
+// Selective-scan forward for sm_100a.
+//
+// Computes, for every (batch b, channel d) row and every timestep t (reference
+// semantics: selective_scan_fwd_kernel.cuh:301-544, selective_scan_interface.py:353-451):
+//   dt_t  = softplus(delta_t + delta_bias_d)                (or delta_t + bias without softplus)
+//   h_t   = exp(dt_t * A_dn) * h_{t-1} + dt_t * u_t * B_nt   for n < dstate
+//   out_t = sum_n C_nt h_t[n] + D_d u_t                     (stored in the input dtype)
+//   out_z = out_t * silu(z_t)                               (when z is given)
+// and, at the end of every kChunkLen-step chunk, x = (prod_t exp(dt_t A_dn), h[n]).
+//
+// Design (B200): one thread owns one (b, d) row and keeps all of its dstate fp32 states
+// in registers, so the recurrence needs no cross-thread scan and y = <C, h> is an
+// in-thread FMA chain.  A CTA owns CH consecutive channels of one (batch, group); tiles
+// of TT timesteps of u / delta / z (rows of the CTA's channels) and of B / C (rows of the
+// group's states, shared by all CH channels) are staged into shared memory with 16-byte
+// cp.async, double-buffered so the next tile streams in while the current one is
+// computed.  B/C are converted to fp32 once per tile into a [t][n] layout that every
+// thread reads with broadcast 16-byte loads.  Outputs are written in place into the
+// staged u / z rows and leave through coalesced 16-byte stores.
+//
+// When batch * dim is too small to fill 148 SMs, the sequence is split into S segments
+// (a multiple of kChunkLen long): a carry pass computes each segment's end state from
+// zero and its summed dt, then the main pass folds the carries of earlier segments into
+// its initial state (h_in = prod(decay) * h_in + H) and runs the full scan.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace mss {
+
+template <int NS> struct FwdCfg {
+    static constexpr int CH = NS <= 16 ? 128 : 64;  // channels (threads) per CTA
+    static constexpr int TT = 32;                   // timesteps per staged tile
+    static constexpr int MINB = NS <= 16 ? 4 : 1;
+};
+
+template <typename T, int NS, bool HAS_Z, bool CARRY>
+struct FwdLayout {
+    static constexpr int CH = FwdCfg<NS>::CH;
+    static constexpr int TT = FwdCfg<NS>::TT;
+    static constexpr int RP = TT * (int)sizeof(T) + 16;  // padded row pitch (conflict-free 16-B reads)
+    static constexpr int NCH_ARR = CARRY ? 2 : (HAS_Z ? 3 : 2);  // u, delta, (z)
+    static constexpr int NST_ARR = CARRY ? 1 : 2;                // B, (C)
+    static constexpr int NROWS = CH * NCH_ARR + NS * NST_ARR;
+    static constexpr int BUF = NROWS * RP;
+    static constexpr int BCW = NS * NST_ARR;  // floats per timestep in the fp32 B/C tile
+    static constexpr int U_OFF = 0, DT_OFF = CH * RP, Z_OFF = 2 * CH * RP;
+    static constexpr int B_OFF = CH * NCH_ARR * RP, C_OFF = B_OFF + NS * RP;
+    static constexpr int SMEM = 2 * BUF + TT * BCW * 4;
+};
+
+template <typename T, int NS, bool HAS_Z, bool CARRY>
+__global__ void __launch_bounds__(FwdCfg<NS>::CH, FwdCfg<NS>::MINB) ss_fwd_kernel(const FwdParams p) {
+    using Ly = FwdLayout<T, NS, HAS_Z, CARRY>;
+    constexpr int CH = Ly::CH, TT = Ly::TT, RP = Ly::RP, BCW = Ly::BCW;
+    extern __shared__ __align__(16) char smem[];
+    float *bc = reinterpret_cast<float *>(smem + 2 * Ly::BUF);
+
+    const int tid = threadIdx.x;
+    const int g = blockIdx.x / p.tiles_per_group;
+    const int tile = blockIdx.x - g * p.tiles_per_group;
+    const int s = blockIdx.y;
+    const int b = blockIdx.z;
+    const int cg0 = tile * CH;                 // first channel of this CTA within its group
+    const int c0 = g * p.dpg + cg0;            // first channel overall
+    const int nvalid_ch = min(CH, p.dpg - cg0);
+    const bool valid = tid < nvalid_ch;
+    const int d = c0 + (valid ? tid : 0);
+    const int64_t L = p.seqlen;
+    const int64_t t_begin = (int64_t)s * p.seg_len;
+    const int64_t t_end = min(L, t_begin + (int64_t)p.seg_len);
+    const bool aligned = p.aligned != 0;
+
+    float A2[NS];
+#pragma unroll
+    for (int n = 0; n < NS; ++n)
+        A2[n] = (valid && n < p.dstate) ? p.A[(int64_t)d * p.A_ds + (int64_t)n * p.A_ns] * kLog2e : 0.f;
+    const float Dv = (p.D != nullptr && valid) ? p.D[(int64_t)d * p.D_s] : 0.f;
+    const float bias = (p.delta_bias != nullptr && valid) ? p.delta_bias[(int64_t)d * p.delta_bias_s] : 0.f;
+
+    float h[NS];
+#pragma unroll
+    for (int n = 0; n < NS; ++n) h[n] = 0.f;
+    float cum = 0.f;  // sum of dt since t = 0 (main pass) or since the segment start (carry pass)
+    const int64_t row = (int64_t)b * p.dim + d;
+    if (!CARRY && s > 0 && valid) {
+        for (int sp = 0; sp < s; ++sp) {
+            const float dts = p.ws_dts[row * p.n_seg + sp];
+            const float *H = p.ws_h + (row * p.n_seg + sp) * NS;
+#pragma unroll
+            for (int n = 0; n < NS; ++n) h[n] = fmaf(ex2(A2[n] * dts), h[n], H[n]);
+            cum += dts;
+        }
+    }
+
+    const T *gu = reinterpret_cast<const T *>(p.u) + (int64_t)b * p.u_bs + (int64_t)c0 * p.u_ds;
+    const T *gdt = reinterpret_cast<const T *>(p.delta) + (int64_t)b * p.delta_bs + (int64_t)c0 * p.delta_ds;
+    const T *gz = HAS_Z ? reinterpret_cast<const T *>(p.z) + (int64_t)b * p.z_bs + (int64_t)c0 * p.z_ds : nullptr;
+    const T *gB = reinterpret_cast<const T *>(p.B) + (int64_t)b * p.B_bs + (int64_t)g * p.B_gs;
+    const T *gC = reinterpret_cast<const T *>(p.C) + (int64_t)b * p.C_bs + (int64_t)g * p.C_gs;
+
+    auto stage = [&](int buf, int64_t t0) {
+        char *rb = smem + buf * Ly::BUF;
+        const int tv = (int)min((int64_t)TT, t_end - t0);
+        stage_tile<T, TT>(rb + Ly::U_OFF, RP, gu, p.u_ds, CH, nvalid_ch, t0, tv, aligned, tid, CH);
+        stage_tile<T, TT>(rb + Ly::DT_OFF, RP, gdt, p.delta_ds, CH, nvalid_ch, t0, tv, aligned, tid, CH);
+        if constexpr (HAS_Z && !CARRY)
+            stage_tile<T, TT>(rb + Ly::Z_OFF, RP, gz, p.z_ds, CH, nvalid_ch, t0, tv, aligned, tid, CH);
+        stage_tile<T, TT>(rb + Ly::B_OFF, RP, gB, p.B_ns, NS, p.dstate, t0, tv, aligned, tid, CH);
+        if constexpr (!CARRY)
+            stage_tile<T, TT>(rb + Ly::C_OFF, RP, gC, p.C_ns, NS, p.dstate, t0, tv, aligned, tid, CH);
+    };
+
+    const int ntiles = (int)((t_end - t_begin + TT - 1) / TT);
+    if (ntiles > 0) stage(0, t_begin);
+    cp_async_commit();
+    for (int it = 0; it < ntiles; ++it) {
+        const int64_t t0 = t_begin + (int64_t)it * TT;
+        const int tv = (int)min((int64_t)TT, t_end - t0);
+        if (it + 1 < ntiles) {
+            stage((it + 1) & 1, t0 + TT);
+            cp_async_commit();
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        char *rb = smem + (it & 1) * Ly::BUF;
+        // B / C tile -> fp32 [t][n] (C after B), once per CTA.
+        for (int i = tid; i < TT * NS; i += CH) {
+            const int n = i % NS, t = i / NS;
+            bc[t * BCW + n] = to_f<T>(reinterpret_cast<const T *>(rb + Ly::B_OFF + n * RP)[t]);
+            if constexpr (!CARRY)
+                bc[t * BCW + NS + n] = to_f<T>(reinterpret_cast<const T *>(rb + Ly::C_OFF + n * RP)[t]);
+        }
+        __syncthreads();
+
+        T *ur = reinterpret_cast<T *>(rb + Ly::U_OFF + tid * RP);
+        const T *dr = reinterpret_cast<const T *>(rb + Ly::DT_OFF + tid * RP);
+#pragma unroll 1
+        for (int g8 = 0; g8 < TT; g8 += 8) {
+            float uf[8], dv[8], dtu[8];
+            Vec8<T>::load(ur + g8, uf);
+            Vec8<T>::load(dr + g8, dv);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                float v = dv[j] + bias;
+                if (p.softplus) v = softplus20(v);
+                v = (g8 + j < tv) ? v : 0.f;  // padded steps: decay 1, input 0
+                dv[j] = v;
+                dtu[j] = v * uf[j];
+                cum += v;
+            }
+            float y[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float4 *bcr = reinterpret_cast<const float4 *>(bc + (g8 + j) * BCW);
+                float acc = 0.f;
+#pragma unroll
+                for (int q = 0; q < NS / 4; ++q) {
+                    const float4 bb = bcr[q];
+                    const float bv[4] = {bb.x, bb.y, bb.z, bb.w};
+                    if constexpr (CARRY) {
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            const int n = 4 * q + k;
+                            h[n] = fmaf(ex2(dv[j] * A2[n]), h[n], dtu[j] * bv[k]);
+                        }
+                    } else {
+                        const float4 cc = bcr[NS / 4 + q];
+                        const float cv[4] = {cc.x, cc.y, cc.z, cc.w};
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            const int n = 4 * q + k;
+                            h[n] = fmaf(ex2(dv[j] * A2[n]), h[n], dtu[j] * bv[k]);
+                            acc = fmaf(cv[k], h[n], acc);
+                        }
+                    }
+                }
+                y[j] = acc;
+            }
+            if constexpr (!CARRY) {
+                float o[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) o[j] = fmaf(Dv, uf[j], y[j]);
+                Vec8<T>::store(ur + g8, o);  // out, in place of u
+                if constexpr (HAS_Z) {
+                    T *zr = reinterpret_cast<T *>(rb + Ly::Z_OFF + tid * RP);
+                    float zf[8];
+                    Vec8<T>::load(zr + g8, zf);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) zf[j] = o[j] * zf[j] * sigmoidf_(zf[j]);
+                    Vec8<T>::store(zr + g8, zf);  // out_z, in place of z
+                }
+            }
+        }
+        if constexpr (!CARRY) {
+            const int64_t te = t0 + tv;
+            if (valid && (te % kChunkLen == 0 || te == L)) {
+                const int64_t k = (te - 1) / kChunkLen;
+                float *xr = p.x + (row * p.n_chunks + k) * 2 * p.dstate;
+#pragma unroll
+                for (int n = 0; n < NS; ++n)
+                    if (n < p.dstate) {
+                        xr[2 * n] = ex2(A2[n] * cum);
+                        xr[2 * n + 1] = h[n];
+                    }
+            }
+            __syncthreads();
+            T *go = reinterpret_cast<T *>(p.out) + (int64_t)b * p.out_bs + (int64_t)c0 * p.out_ds;
+            store_tile<T, TT>(go, p.out_ds, rb + Ly::U_OFF, RP, nvalid_ch, t0, tv, aligned, tid, CH);
+            if constexpr (HAS_Z) {
+                T *goz = reinterpret_cast<T *>(p.out_z) + (int64_t)b * p.out_z_bs + (int64_t)c0 * p.out_z_ds;
+                store_tile<T, TT>(goz, p.out_z_ds, rb + Ly::Z_OFF, RP, nvalid_ch, t0, tv, aligned, tid, CH);
+            }
+        }
+        __syncthreads();
+    }
+    if (CARRY && valid) {
+        float *H = p.ws_h + (row * p.n_seg + s) * NS;
+#pragma unroll
+        for (int n = 0; n < NS; ++n) H[n] = h[n];
+        p.ws_dts[row * p.n_seg + s] = cum;
+    }
+}
+
+template <typename T, int NS, bool HAS_Z, bool CARRY>
+static cudaError_t launch_one(const FwdParams &p, dim3 grid, cudaStream_t st) {
+    using Ly = FwdLayout<T, NS, HAS_Z, CARRY>;
+    auto kern = ss_fwd_kernel<T, NS, HAS_Z, CARRY>;
+    static bool configured = false;  // idempotent attribute set; racing threads set the same value
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Ly::SMEM);
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    kern<<<grid, Ly::CH, Ly::SMEM, st>>>(p);
+    return cudaGetLastError();
+}
+
+template <typename T, int NS>
+static cudaError_t launch_ns(FwdParams p, bool has_z, cudaStream_t st) {
+    constexpr int CH = FwdCfg<NS>::CH;
+    p.tiles_per_group = (p.dpg + CH - 1) / CH;
+    dim3 grid(p.tiles_per_group * p.n_groups, p.n_seg, p.batch);
+    cudaError_t e = cudaSuccess;
+    if (p.n_seg > 1) {
+        dim3 gc(grid.x, p.n_seg - 1, grid.z);
+        e = launch_one<T, NS, false, true>(p, gc, st);
+        if (e != cudaSuccess) return e;
+    }
+    if (has_z) return launch_one<T, NS, true, false>(p, grid, st);
+    return launch_one<T, NS, false, false>(p, grid, st);
+}
+
+int fwd_state_pad(int dstate) {
+    if (dstate <= 4) return 4;
+    if (dstate <= 8) return 8;
+    if (dstate <= 16) return 16;
+    if (dstate <= 32) return 32;
+    return 64;
+}
+
+int fwd_channels_per_cta(int dstate) { return fwd_state_pad(dstate) <= 16 ? 128 : 64; }
+
+template <typename T>
+static cudaError_t launch_t(const FwdParams &p, bool has_z, cudaStream_t st) {
+    switch (fwd_state_pad(p.dstate)) {
+        case 4: return launch_ns<T, 4>(p, has_z, st);
+        case 8: return launch_ns<T, 8>(p, has_z, st);
+        case 16: return launch_ns<T, 16>(p, has_z, st);
+        case 32: return launch_ns<T, 32>(p, has_z, st);
+        default: return launch_ns<T, 64>(p, has_z, st);
+    }
+}
+
+cudaError_t launch_ss_fwd(const FwdParams &p, int itype, bool has_z, cudaStream_t st) {
+    switch (itype) {
+        case MSS_F32: return launch_t<float>(p, has_z, st);
+        case MSS_F16: return launch_t<__half>(p, has_z, st);
+        default: return launch_t<__nv_bfloat16>(p, has_z, st);
+    }
+}
+
+}  // namespace mss

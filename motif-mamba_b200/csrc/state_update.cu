@@ -1,0 +1,84 @@
+// Single-token SSM state update (decode) for sm_100a.
+//
+// Semantics of mamba_ssm's selective_state_update, which the reference calls at
+// mamba_ssm/modules/mamba_simplemotif.py:396-399 (the Triton source is not in the
+// reference); restated from the module's torch fallback (:367-376):
+//   dt    = softplus(dt + dt_bias)                      (if dt_softplus)
+//   state = state * exp(dt * A) + dt * B * x            (in place, state dtype)
+//   out   = sum_n state[n] * C[n] + D * x,   out *= silu(z)
+// One thread per (batch, channel) keeps its dstate states in registers (fp32 math).
+// Decode is latency bound (a few MB per layer), so the kernel is one short launch.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace mss {
+
+template <typename T, typename ST, int NS>
+__global__ void __launch_bounds__(128) state_update_kernel(const ssm_state_update_args a) {
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i >= a.batch * a.dim) return;
+    const int64_t b = i / a.dim, d = i - b * a.dim;
+    const int64_t g = d / (a.dim / a.n_groups);
+    const T *X = reinterpret_cast<const T *>(a.x);
+    const T *DT = reinterpret_cast<const T *>(a.dt);
+    const float xv = to_f<T>(X[b * a.x_bs + d]);
+    float dt = to_f<T>(DT[b * a.dt_bs + d]);
+    if (a.dt_bias) dt += a.dt_bias[d];
+    if (a.dt_softplus) dt = softplus20(dt);
+    const T *Bp = reinterpret_cast<const T *>(a.B) + b * a.B_bs + g * a.B_gs;
+    const T *Cp = reinterpret_cast<const T *>(a.C) + b * a.C_bs + g * a.C_gs;
+    ST *st = reinterpret_cast<ST *>(a.state) + b * a.st_bs + d * a.st_ds;
+    const float dtx = dt * xv;
+    float y = 0.f;
+#pragma unroll
+    for (int n = 0; n < NS; ++n) {
+        if (n < a.dstate) {
+            const float A = a.A[d * a.A_ds + n * a.A_ns];
+            float s = to_f<ST>(st[n * a.st_ns]);
+            s = fmaf(ex2(dt * A * kLog2e), s, dtx * to_f<T>(Bp[n]));
+            const ST sr = from_f<ST>(s);
+            st[n * a.st_ns] = sr;
+            y = fmaf(to_f<ST>(sr), to_f<T>(Cp[n]), y);
+        }
+    }
+    if (a.D) y = fmaf(a.D[d], xv, y);
+    if (a.z) {
+        const float zv = to_f<T>(reinterpret_cast<const T *>(a.z)[b * a.z_bs + d]);
+        y *= zv * sigmoidf_(zv);
+    }
+    reinterpret_cast<T *>(a.out)[b * a.out_bs + d] = from_f<T>(y);
+}
+
+template <typename T, typename ST>
+static cudaError_t su_st(const ssm_state_update_args &a, cudaStream_t st) {
+    const int64_t n = a.batch * a.dim;
+    const int threads = 128;
+    const unsigned blocks = (unsigned)((n + threads - 1) / threads);
+    if (n == 0) return cudaSuccess;
+    if (a.dstate <= 16)
+        state_update_kernel<T, ST, 16><<<blocks, threads, 0, st>>>(a);
+    else if (a.dstate <= 32)
+        state_update_kernel<T, ST, 32><<<blocks, threads, 0, st>>>(a);
+    else if (a.dstate <= 64)
+        state_update_kernel<T, ST, 64><<<blocks, threads, 0, st>>>(a);
+    else
+        state_update_kernel<T, ST, 256><<<blocks, threads, 0, st>>>(a);
+    return cudaGetLastError();
+}
+template <typename T>
+static cudaError_t su_t(const ssm_state_update_args &a, cudaStream_t st) {
+    switch (a.stype) {
+        case MSS_F32: return su_st<T, float>(a, st);
+        case MSS_F16: return su_st<T, __half>(a, st);
+        default: return su_st<T, __nv_bfloat16>(a, st);
+    }
+}
+cudaError_t launch_state_update(const ssm_state_update_args &a, cudaStream_t st) {
+    switch (a.itype) {
+        case MSS_F32: return su_t<float>(a, st);
+        case MSS_F16: return su_t<__half>(a, st);
+        default: return su_t<__nv_bfloat16>(a, st);
+    }
+}
+
+}  // namespace mss

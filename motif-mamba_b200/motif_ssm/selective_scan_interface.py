@@ -1,0 +1,206 @@
+"""``selective_scan_fn`` and ``mamba_inner_fn`` on the sm_100a kernels.
+
+Same call signatures and autograd contract as the reference's
+``mamba_ssm/ops/selective_scan_interface.py`` (``selective_scan_fn`` :237-259,
+``SelectiveScanFn`` :24-91, ``mamba_inner_fn`` :648-656, ``MambaInnerFn`` :454-645):
+
+* ``selective_scan_fn(u, delta, A, B, C, D=None, z=None, delta_bias=None,
+  delta_softplus=False, return_last_state=False)`` returns ``out`` (z-gated when z is
+  given) and optionally ``last_state`` (batch, dim, dstate) fp32, which carries no
+  gradient;
+* ``mamba_inner_fn(xz, conv1d_weight, conv1d_bias, x_proj_weight, delta_proj_weight,
+  out_proj_weight, out_proj_bias, A, B=None, C=None, D=None, delta_bias=None,
+  B_proj_bias=None, C_proj_bias=None, delta_softplus=True, checkpoint_lvl=1)`` fuses
+  conv1d+SiLU -> x_proj -> dt_proj -> scan -> out_proj; with ``checkpoint_lvl=1`` the
+  backward recomputes the conv output and delta instead of saving them.
+
+The GEMMs (x_proj, dt_proj, out_proj and their gradients) are cuBLAS calls through
+torch; the conv, the scan and its backward are this library's kernels.
+"""
+import torch
+import torch.nn.functional as F
+
+from . import selective_scan_cuda
+from .causal_conv1d import causal_conv1d_bwd_function, causal_conv1d_fwd_function
+
+
+def _last_dim_contig(t):
+    return t if (t is None or t.stride(-1) == 1) else t.contiguous()
+
+
+class SelectiveScanFn(torch.autograd.Function):
+
+    @staticmethod
+    def forward(ctx, u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softplus=False,
+                return_last_state=False):
+        u, delta, B, C, z = (_last_dim_contig(t) for t in (u, delta, B, C, z))
+        if D is not None:
+            D = D.contiguous()
+        ctx.squeeze_B = B.dim() == 3
+        ctx.squeeze_C = C.dim() == 3
+        if ctx.squeeze_B:
+            B = B.unsqueeze(1)
+        if ctx.squeeze_C:
+            C = C.unsqueeze(1)
+        out, x, *rest = selective_scan_cuda.fwd(u, delta, A, B, C, D=D, z=z, delta_bias=delta_bias,
+                                                delta_softplus=delta_softplus)
+        ctx.delta_softplus = delta_softplus
+        ctx.has_z = z is not None
+        last_state = x[:, :, -1, 1::2]
+        if ctx.has_z:
+            ctx.save_for_backward(u, delta, A, B, C, D, z, delta_bias, x, out)
+            result = rest[0]
+        else:
+            ctx.save_for_backward(u, delta, A, B, C, D, delta_bias, x)
+            result = out
+        ctx.mark_non_differentiable(last_state)
+        return (result, last_state) if return_last_state else result
+
+    @staticmethod
+    def backward(ctx, dout, *unused):
+        if ctx.has_z:
+            u, delta, A, B, C, D, z, delta_bias, x, out = ctx.saved_tensors
+        else:
+            u, delta, A, B, C, D, delta_bias, x = ctx.saved_tensors
+            z = out = None
+        dout = _last_dim_contig(dout)
+        du, ddelta, dA, dB, dC, dD, ddelta_bias, *rest = selective_scan_cuda.bwd(
+            u, delta, A, B, C, D=D, z=z, delta_bias=delta_bias, dout=dout, x=x, out=out, dz=None,
+            delta_softplus=ctx.delta_softplus, recompute_out_z=False)
+        dz = rest[0] if ctx.has_z else None
+        if ctx.squeeze_B:
+            dB = dB.squeeze(1)
+        if ctx.squeeze_C:
+            dC = dC.squeeze(1)
+        return (du, ddelta, dA, dB, dC, dD if D is not None else None, dz,
+                ddelta_bias if delta_bias is not None else None, None, None)
+
+
+def selective_scan_fn(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softplus=False,
+                      return_last_state=False, P=None, Q=None, gamma=None):
+    """If ``return_last_state`` is True returns ``(out, last_state)``; ``last_state`` is
+    (batch, dim, dstate) and receives no gradient."""
+    if P is not None or Q is not None or gamma is not None:
+        raise NotImplementedError("selective_scan_fn: the P/Q (motif low-rank) path is not built in this library")
+    return SelectiveScanFn.apply(u, delta, A, B, C, D, z, delta_bias, delta_softplus, return_last_state)
+
+
+class MambaInnerFn(torch.autograd.Function):
+
+    @staticmethod
+    def forward(ctx, xz, conv1d_weight, conv1d_bias, x_proj_weight, delta_proj_weight, out_proj_weight,
+                out_proj_bias, A, B=None, C=None, D=None, delta_bias=None, B_proj_bias=None,
+                C_proj_bias=None, delta_softplus=True, checkpoint_lvl=1):
+        assert checkpoint_lvl in (0, 1)
+        if A.is_complex():
+            raise NotImplementedError("mamba_inner_fn: complex A is not supported by this library")
+        L = xz.shape[-1]
+        rank = delta_proj_weight.shape[1]
+        d_state = A.shape[-1]
+        if torch.is_autocast_enabled():
+            dt = torch.get_autocast_dtype("cuda")
+            x_proj_weight = x_proj_weight.to(dt)
+            delta_proj_weight = delta_proj_weight.to(dt)
+            out_proj_weight = out_proj_weight.to(dt)
+            out_proj_bias = out_proj_bias.to(dt) if out_proj_bias is not None else None
+        xz = _last_dim_contig(xz)
+        w_conv = conv1d_weight.reshape(conv1d_weight.shape[0], conv1d_weight.shape[-1])
+        x, z = xz.chunk(2, dim=1)
+        conv1d_bias = conv1d_bias.contiguous() if conv1d_bias is not None else None
+        conv_out = causal_conv1d_fwd_function(x, w_conv, conv1d_bias, None, None, None, True)
+        # (b, d, l) -> (b*l, d) rows for x_proj; delta comes back as a (b, d, l) view of a
+        # (d, b*l) product, so l stays unit-stride without a transpose copy.
+        x_dbl = F.linear(conv_out.transpose(1, 2).reshape(-1, conv_out.shape[1]), x_proj_weight)
+        delta = (delta_proj_weight @ x_dbl[:, :rank].t()).view(-1, xz.shape[0], L).transpose(0, 1)
+        ctx.is_variable_B = B is None
+        ctx.is_variable_C = C is None
+        ctx.B_proj_bias_is_None = B_proj_bias is None
+        ctx.C_proj_bias_is_None = C_proj_bias is None
+        if B is None:
+            B = x_dbl[:, rank:rank + d_state]
+            if B_proj_bias is not None:
+                B = B + B_proj_bias.to(B.dtype)
+            B = B.view(xz.shape[0], L, d_state).transpose(1, 2).unsqueeze(1).contiguous()
+        else:
+            B = _last_dim_contig(B)
+        if C is None:
+            C = x_dbl[:, -d_state:]
+            if C_proj_bias is not None:
+                C = C + C_proj_bias.to(C.dtype)
+            C = C.view(xz.shape[0], L, d_state).transpose(1, 2).unsqueeze(1).contiguous()
+        else:
+            C = _last_dim_contig(C)
+        if D is not None:
+            D = D.contiguous()
+        out, scan_x, out_z = selective_scan_cuda.fwd(conv_out, delta, A, B, C, D=D, z=z, delta_bias=delta_bias,
+                                                     delta_softplus=delta_softplus)
+        ctx.delta_softplus = delta_softplus
+        ctx.out_proj_bias_is_None = out_proj_bias is None
+        ctx.checkpoint_lvl = checkpoint_lvl
+        if checkpoint_lvl >= 1:
+            conv_out, delta = None, None
+        ctx.save_for_backward(xz, w_conv, conv1d_bias, x_dbl, x_proj_weight, delta_proj_weight, out_proj_weight,
+                              conv_out, delta, A, B, C, D, delta_bias, scan_x, out)
+        return F.linear(out_z.transpose(1, 2), out_proj_weight, out_proj_bias)
+
+    @staticmethod
+    def backward(ctx, dout):
+        (xz, w_conv, conv1d_bias, x_dbl, x_proj_weight, delta_proj_weight, out_proj_weight, conv_out, delta,
+         A, B, C, D, delta_bias, scan_x, out) = ctx.saved_tensors
+        L = xz.shape[-1]
+        batch = xz.shape[0]
+        rank = delta_proj_weight.shape[1]
+        d_state = A.shape[-1]
+        x, z = xz.chunk(2, dim=1)
+        dout = _last_dim_contig(dout)
+        if ctx.checkpoint_lvl == 1:
+            conv_out = causal_conv1d_fwd_function(x, w_conv, conv1d_bias, None, None, None, True)
+            delta = (delta_proj_weight @ x_dbl[:, :rank].t()).view(-1, batch, L).transpose(0, 1)
+        dxz = torch.empty_like(xz)
+        dx, dz = dxz.chunk(2, dim=1)
+        dout2 = dout.reshape(-1, dout.shape[-1]).t()              # (e, b*l)
+        dout_y = (out_proj_weight.t() @ dout2).view(-1, batch, L).transpose(0, 1)
+        dconv_out, ddelta, dA, dB, dC, dD, ddelta_bias, dz, out_z = selective_scan_cuda.bwd(
+            conv_out, delta, A, B, C, D=D, z=z, delta_bias=delta_bias, dout=dout_y, x=scan_x, out=out, dz=dz,
+            delta_softplus=ctx.delta_softplus, recompute_out_z=True)
+        out_z_rows = out_z.transpose(0, 1).reshape(out_z.shape[1], -1)  # (d, b*l)
+        dout_proj_weight = dout2 @ out_z_rows.t()
+        dout_proj_bias = dout.sum(dim=(0, 1)) if not ctx.out_proj_bias_is_None else None
+        dx_dbl = torch.empty_like(x_dbl)
+        dB_proj_bias = dC_proj_bias = None
+        if ctx.is_variable_B:
+            dB_rows = dB.squeeze(1).transpose(1, 2).reshape(-1, d_state)
+            dB_proj_bias = dB_rows.sum(0) if not ctx.B_proj_bias_is_None else None
+            dx_dbl[:, rank:rank + d_state] = dB_rows
+            dB = None
+        if ctx.is_variable_C:
+            dC_rows = dC.squeeze(1).transpose(1, 2).reshape(-1, d_state)
+            dC_proj_bias = dC_rows.sum(0) if not ctx.C_proj_bias_is_None else None
+            dx_dbl[:, -d_state:] = dC_rows
+            dC = None
+        ddelta_rows = ddelta.transpose(0, 1).reshape(ddelta.shape[1], -1)  # (d, b*l)
+        ddelta_proj_weight = ddelta_rows @ x_dbl[:, :rank]
+        dx_dbl[:, :rank] = ddelta_rows.t() @ delta_proj_weight
+        conv_rows = conv_out.transpose(1, 2).reshape(-1, conv_out.shape[1])  # (b*l, d)
+        dx_proj_weight = dx_dbl.t() @ conv_rows
+        dconv_rows = dconv_out.transpose(0, 1).reshape(dconv_out.shape[1], -1)  # (d, b*l), a copy
+        dconv_rows = torch.addmm(dconv_rows, x_proj_weight.t(), dx_dbl.t())
+        dconv_out = dconv_rows.view(-1, batch, L).transpose(0, 1)
+        dx, dconv_w, dconv_b, _ = causal_conv1d_bwd_function(x, w_conv, conv1d_bias, dconv_out, None, None, None,
+                                                             dx, False, True)
+        dconv_b = dconv_b if conv1d_bias is not None else None
+        dconv_w = dconv_w.unsqueeze(1)
+        return (dxz, dconv_w, dconv_b, dx_proj_weight, ddelta_proj_weight, dout_proj_weight, dout_proj_bias,
+                dA, dB, dC, dD, ddelta_bias if delta_bias is not None else None, dB_proj_bias, dC_proj_bias,
+                None, None)
+
+
+def mamba_inner_fn(xz, conv1d_weight, conv1d_bias, x_proj_weight, delta_proj_weight, out_proj_weight,
+                   out_proj_bias, A, B=None, C=None, D=None, delta_bias=None, B_proj_bias=None,
+                   C_proj_bias=None, delta_softplus=True, checkpoint_lvl=1, b_rms_weight=None,
+                   c_rms_weight=None, dt_rms_weight=None, b_c_dt_rms_eps=1e-6):
+    if b_rms_weight is not None or c_rms_weight is not None or dt_rms_weight is not None:
+        raise NotImplementedError("mamba_inner_fn: the B/C/dt RMSNorm options are not built in this library")
+    return MambaInnerFn.apply(xz, conv1d_weight, conv1d_bias, x_proj_weight, delta_proj_weight, out_proj_weight,
+                              out_proj_bias, A, B, C, D, delta_bias, B_proj_bias, C_proj_bias, delta_softplus,
+                              checkpoint_lvl)

@@ -1,0 +1,69 @@
+"""Drop-in for ``mamba_ssm.ops.triton.selective_state_update.selective_state_update``
+(called at ``mamba_ssm/modules/mamba_simplemotif.py:396-399``), on ``libmotif_ssm.so``.
+
+state (batch, dim, dstate) is updated in place; returns out (batch, dim).
+"""
+import ctypes
+
+import torch
+
+from . import _lib
+from ._lib import lib, check
+from .selective_scan_cuda import _itype, _ptr, _stream, _req
+
+
+def selective_state_update(state, x, dt, A, B, C, D=None, z=None, dt_bias=None, dt_softplus=False,
+                           state_batch_indices=None):
+    if state_batch_indices is not None:
+        raise NotImplementedError("selective_state_update: state_batch_indices is not supported")
+    if state.dim() != 3:
+        raise NotImplementedError("selective_state_update: only the (batch, dim, dstate) layout is supported")
+    batch, dim, dstate = state.shape
+    _req(x.shape == (batch, dim) and dt.shape == (batch, dim), "x and dt must be (batch, dim)")
+    _req(x.dtype == dt.dtype, "x and dt must share a dtype")
+    _req(A.shape == (dim, dstate) and A.dtype == torch.float32, "A must be float32 (dim, dstate)")
+    if B.dim() == 2:
+        B = B.unsqueeze(1)
+    if C.dim() == 2:
+        C = C.unsqueeze(1)
+    n_groups = B.shape[1]
+    _req(B.shape == (batch, n_groups, dstate) and C.shape == (batch, n_groups, dstate),
+         "B and C must be (batch, dstate) or (batch, n_groups, dstate)")
+    if B.dtype != x.dtype:
+        B = B.to(x.dtype)
+    if C.dtype != x.dtype:
+        C = C.to(x.dtype)
+    if B.stride(-1) != 1:
+        B = B.contiguous()
+    if C.stride(-1) != 1:
+        C = C.contiguous()
+    for t in (x, dt):
+        _req(t.stride(-1) == 1, "x and dt must have unit stride in the last dimension")
+    if D is not None:
+        D = D.float().contiguous()
+        _req(D.shape == (dim,), "D must be (dim,)")
+    if dt_bias is not None:
+        dt_bias = dt_bias.float().contiguous()
+        _req(dt_bias.shape == (dim,), "dt_bias must be (dim,)")
+    if z is not None:
+        _req(z.shape == (batch, dim) and z.stride(-1) == 1, "z must be (batch, dim), unit stride")
+        if z.dtype != x.dtype:
+            z = z.to(x.dtype)
+    out = torch.empty_like(x)
+    a = _lib.StateUpdateArgs()
+    a.batch, a.dim, a.dstate, a.n_groups = batch, dim, dstate, n_groups
+    a.itype, a.stype, a.dt_softplus = _itype(x.dtype), _itype(state.dtype), 1 if dt_softplus else 0
+    a.state, a.st_bs, a.st_ds, a.st_ns = _ptr(state), state.stride(0), state.stride(1), state.stride(2)
+    a.x, a.x_bs = _ptr(x), x.stride(0)
+    a.dt, a.dt_bs = _ptr(dt), dt.stride(0)
+    a.A, a.A_ds, a.A_ns = _ptr(A), A.stride(0), A.stride(1)
+    a.B, a.B_bs, a.B_gs = _ptr(B), B.stride(0), B.stride(1)
+    a.C, a.C_bs, a.C_gs = _ptr(C), C.stride(0), C.stride(1)
+    a.D = _ptr(D)
+    if z is not None:
+        a.z, a.z_bs = _ptr(z), z.stride(0)
+    a.dt_bias = _ptr(dt_bias)
+    a.out, a.out_bs = _ptr(out), out.stride(0)
+    with torch.cuda.device(x.device):
+        check(lib.ssm_state_update(ctypes.byref(a), _stream(x.device)))
+    return out

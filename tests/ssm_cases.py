@@ -1,0 +1,59 @@
+"""Seeded input generators and comparison helpers shared by the tests.
+
+Inputs follow BASELINE config 0 / 4: u, z, B, C ~ N(0, 1); delta ~ N(0, 1) with
+delta_bias = inverse-softplus(U[1e-3, 1e-1]) and softplus on; A = -(1..n) per channel;
+D ~ N(1, 0.1).  Tensors are generated on the CPU from a seeded generator and then
+moved, so the oracle and the kernel see identical values.
+"""
+import torch
+
+
+def make_scan_inputs(batch, dim, seqlen, dstate, dtype=torch.float32, groups=0, has_z=True, has_D=True,
+                     has_bias=True, softplus=True, seed=0, device="cpu"):
+    g = torch.Generator().manual_seed(seed)
+    u = torch.randn(batch, dim, seqlen, generator=g)
+    if softplus:
+        delta = torch.randn(batch, dim, seqlen, generator=g)
+    else:
+        delta = 0.5 * torch.rand(batch, dim, seqlen, generator=g)
+    A = -torch.arange(1, dstate + 1, dtype=torch.float32).repeat(dim, 1).contiguous()
+    G = groups if groups else 1
+    B = torch.randn(batch, G, dstate, seqlen, generator=g)
+    C = torch.randn(batch, G, dstate, seqlen, generator=g)
+    if not groups:
+        B, C = B[:, 0], C[:, 0]
+    D = (1.0 + 0.1 * torch.randn(dim, generator=g)) if has_D else None
+    z = torch.randn(batch, dim, seqlen, generator=g) if has_z else None
+    bias = torch.log(torch.expm1(torch.rand(dim, generator=g) * (0.1 - 1e-3) + 1e-3)) if has_bias else None
+    dout = torch.randn(batch, dim, seqlen, generator=g)
+    cast = lambda t: None if t is None else t.to(dtype).to(device)
+    keep = lambda t: None if t is None else t.float().to(device)
+    inputs = dict(u=cast(u), delta=cast(delta), A=keep(A), B=cast(B), C=cast(C), D=keep(D), z=cast(z),
+                  delta_bias=keep(bias))
+    return inputs, cast(dout)
+
+
+def tol(dtype):
+    """Tolerances of the north star: 1e-3 for fp32 I/O, 2e-2 for bf16/fp16 I/O (fp32 math)."""
+    return 1e-3 if dtype == torch.float32 else 2e-2
+
+
+def assert_close(actual, expected, rtol, atol, name=""):
+    """|a - e| <= atol * max(1, max|e|) + rtol * |e| elementwise.
+
+    The absolute term is scaled by the tensor's magnitude so that sums over thousands of
+    channels (dB, dC, dA) are held to the same relative standard as elementwise outputs.
+    """
+    a = actual.detach().float().cpu()
+    e = expected.detach().float().cpu()
+    assert a.shape == e.shape, f"{name}: shape {tuple(a.shape)} != {tuple(e.shape)}"
+    scale = max(1.0, e.abs().max().item()) if e.numel() else 1.0
+    err = (a - e).abs()
+    bound = atol * scale + rtol * e.abs()
+    bad = err > bound
+    if bad.any():
+        i = int(torch.argmax((err - bound).flatten()))
+        raise AssertionError(
+            f"{name}: {int(bad.sum())}/{e.numel()} elements out of tolerance; worst at flat index {i}: "
+            f"actual {a.flatten()[i].item():.6g} expected {e.flatten()[i].item():.6g} "
+            f"(max abs err {err.max().item():.3g}, scale {scale:.3g})")

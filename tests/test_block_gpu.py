@@ -1,0 +1,140 @@
+"""Parity of the conv1d, decode-step and fused-block kernels (through the C ABI) with
+the CPU oracle and the reference's golden fixtures."""
+import os
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from oracle import ssm_oracle as O
+from ssm_cases import assert_close, tol
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+DEV = "cuda"
+
+
+@pytest.mark.parametrize("batch,dim,seqlen,width,dtype,wdtype,bias,silu", [
+    (2, 64, 300, 4, torch.float32, torch.float32, True, True),
+    (2, 64, 257, 4, torch.bfloat16, torch.bfloat16, True, True),
+    (1, 33, 1, 4, torch.float32, torch.float32, False, True),
+    (3, 16, 77, 3, torch.float16, torch.float32, True, False),
+    (2, 8, 40, 2, torch.bfloat16, torch.float32, True, True),
+])
+def test_causal_conv1d_fwd_bwd(batch, dim, seqlen, width, dtype, wdtype, bias, silu):
+    from motif_ssm import causal_conv1d_fn
+    g = torch.Generator().manual_seed(seqlen)
+    x = torch.randn(batch, dim, seqlen, generator=g).to(dtype)
+    w = (0.5 * torch.randn(dim, width, generator=g)).to(wdtype)
+    b = (0.1 * torch.randn(dim, generator=g)).to(wdtype) if bias else None
+    dout = torch.randn(batch, dim, seqlen, generator=g).to(dtype)
+    act = "silu" if silu else None
+    leaves = [t.clone().requires_grad_(True) if t is not None else None for t in (x, w, b)]
+    ref = O.causal_conv1d_ref(leaves[0], leaves[1], leaves[2], activation=act)
+    ref.backward(dout)
+    dl = [t.to(DEV).clone().requires_grad_(True) if t is not None else None for t in (x, w, b)]
+    out = causal_conv1d_fn(dl[0], dl[1], dl[2], activation=act)
+    out.backward(dout.to(DEV))
+    t = tol(dtype)
+    assert_close(out, ref, t, t, "conv out")
+    assert_close(dl[0].grad, leaves[0].grad, t, t, "conv dx")
+    assert_close(dl[1].grad, leaves[1].grad, t, t, "conv dweight")
+    if bias:
+        assert_close(dl[2].grad, leaves[2].grad, t, t, "conv dbias")
+
+
+def test_conv_update_and_state_update_match_module_golden():
+    """Replays Mambamotif.step's decode steps (golden from the reference's own module)
+    with causal_conv1d_update + selective_state_update on the GPU."""
+    from motif_ssm import causal_conv1d_update, selective_state_update
+    rec = torch.load(os.path.join(GOLD, "module_small.pt"), weights_only=False)
+    sd = {k: v.to(DEV) for k, v in rec["state_dict"].items()}
+    conv_state = rec["conv_state0"].to(DEV).clone()
+    ssm_state = rec["ssm_state0"].to(DEV).clone()
+    W = sd["conv1d.weight"][:, 0, :]
+    dt_rank = sd["dt_proj.weight"].shape[1]
+    n = sd["A_log"].shape[1]
+    A = -torch.exp(sd["A_log"].float())
+    for i in range(rec["step_in"].shape[0]):
+        hs = rec["step_in"][i][:, 0].to(DEV)
+        xz = hs @ sd["in_proj.weight"].t()
+        x, z = xz.chunk(2, dim=-1)
+        x = causal_conv1d_update(x, conv_state, W, sd["conv1d.bias"], "silu")
+        x_db = x @ sd["x_proj.weight"].t()
+        dt, B, C = torch.split(x_db, [dt_rank, n, n], dim=-1)
+        dt = dt @ sd["dt_proj.weight"].t()
+        y = selective_state_update(ssm_state, x, dt, A, B, C, sd["D"], z=z, dt_bias=sd["dt_proj.bias"],
+                                   dt_softplus=True)
+        out = y @ sd["out_proj.weight"].t()
+        assert_close(out, rec["step_out"][i][:, 0], 1e-3, 1e-3, f"step {i} out")
+    assert_close(conv_state, rec["conv_state_final"], 1e-6, 1e-6, "conv_state")
+    assert_close(ssm_state, rec["ssm_state_final"], 1e-3, 1e-3, "ssm_state")
+
+
+@pytest.mark.parametrize("dtype,state_dtype", [(torch.bfloat16, torch.bfloat16), (torch.float32, torch.float32),
+                                               (torch.bfloat16, torch.float32)])
+def test_state_update_decode_config2_shape(dtype, state_dtype):
+    """Decode step at BASELINE config 2's decode shape (batch 64, d_inner 1536, n 16)."""
+    from motif_ssm import selective_state_update
+    batch, dim, n = 64, 1536, 16
+    g = torch.Generator().manual_seed(0)
+    state = torch.randn(batch, dim, n, generator=g).to(state_dtype)
+    x = torch.randn(batch, dim, generator=g).to(dtype)
+    dt = torch.randn(batch, dim, generator=g).to(dtype)
+    A = -torch.arange(1, n + 1, dtype=torch.float32).repeat(dim, 1)
+    B = torch.randn(batch, n, generator=g).to(dtype)
+    C = torch.randn(batch, n, generator=g).to(dtype)
+    D = torch.randn(dim, generator=g)
+    z = torch.randn(batch, dim, generator=g).to(dtype)
+    dt_bias = torch.randn(dim, generator=g)
+    ref_state = state.clone()
+    ref = O.selective_state_update_ref(ref_state, x, dt, A, B, C, D, z=z, dt_bias=dt_bias, dt_softplus=True)
+    st = state.to(DEV)
+    out = selective_state_update(st, x.to(DEV), dt.to(DEV), A.to(DEV), B.to(DEV), C.to(DEV), D.to(DEV),
+                                 z=z.to(DEV), dt_bias=dt_bias.to(DEV), dt_softplus=True)
+    t = tol(dtype if state_dtype == torch.float32 else torch.bfloat16)
+    assert_close(out, ref, t, t, "y")
+    assert_close(st, ref_state, t, t, "state")
+
+
+def test_mamba_inner_matches_reference_golden():
+    from motif_ssm import mamba_inner_fn
+    rec = torch.load(os.path.join(GOLD, "inner_small.pt"), weights_only=False)
+    leaves = {k: v.to(DEV).clone().requires_grad_(True) for k, v in rec["inputs"].items()}
+    out = mamba_inner_fn(leaves["xz"], leaves["conv1d_weight"], leaves["conv1d_bias"], leaves["x_proj_weight"],
+                         leaves["delta_proj_weight"], leaves["out_proj_weight"], leaves["out_proj_bias"],
+                         leaves["A"], None, None, leaves["D"], delta_bias=leaves["delta_bias"],
+                         delta_softplus=True)
+    out.backward(rec["dout"].to(DEV))
+    assert_close(out, rec["out"], 1e-3, 1e-3, "inner out")
+    for k, g in rec["grads"].items():
+        assert_close(leaves[k].grad, g, 1e-3, 1e-3, f"inner d{k}")
+
+
+def test_mamba_inner_bf16_config1_block_vs_oracle():
+    """BASELINE config 1's block (d_model 768, d_inner 1536, n 16, dt_rank 48) in bf16,
+    at batch 1 x seqlen 512 so the CPU oracle finishes in seconds."""
+    from motif_ssm import mamba_inner_fn
+    batch, seqlen, d_model, d_inner, n, rank = 1, 512, 768, 1536, 16, 48
+    g = torch.Generator().manual_seed(1)
+    p = dict(
+        xz=torch.randn(batch, 2 * d_inner, seqlen, generator=g),
+        conv1d_weight=0.02 * torch.randn(d_inner, 1, 4, generator=g),
+        conv1d_bias=0.02 * torch.randn(d_inner, generator=g),
+        x_proj_weight=0.02 * torch.randn(rank + 2 * n, d_inner, generator=g),
+        delta_proj_weight=(rank ** -0.5) * (2 * torch.rand(d_inner, rank, generator=g) - 1),
+        out_proj_weight=0.02 * torch.randn(d_model, d_inner, generator=g),
+    )
+    A = -torch.arange(1, n + 1, dtype=torch.float32).repeat(d_inner, 1)
+    D = torch.ones(d_inner)
+    bias = torch.log(torch.expm1(torch.exp(torch.rand(d_inner, generator=g) * (2.302585 * 2) - 6.907755)))
+    pb = {k: v.bfloat16() for k, v in p.items()}
+    ref = O.mamba_inner_ref(pb["xz"].float(), pb["conv1d_weight"].float(), pb["conv1d_bias"].float(),
+                            pb["x_proj_weight"].float(), pb["delta_proj_weight"].float(),
+                            pb["out_proj_weight"].float(), None, A, None, None, D, delta_bias=bias)
+    with torch.no_grad():
+        out = mamba_inner_fn(*(pb[k].to(DEV) for k in ("xz", "conv1d_weight", "conv1d_bias", "x_proj_weight",
+                                                         "delta_proj_weight", "out_proj_weight")),
+                             None, A.to(DEV), None, None, D.to(DEV), delta_bias=bias.to(DEV))
+    assert out.dtype == torch.bfloat16
+    assert_close(out, ref, 2e-2, 2e-2, "config-1 block out")
