@@ -223,7 +223,14 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the per-GPU batch (profiling a smaller case of the same kernels)")
+    ap.add_argument("--seqlen", type=int, default=None, help="override the sequence length")
     args = ap.parse_args()
+    if args.batch:
+        CFG["batch"] = args.batch
+    if args.seqlen:
+        CFG["seqlen"] = args.seqlen
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference(args)

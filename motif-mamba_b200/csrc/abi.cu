@@ -114,13 +114,15 @@ struct BwdShape {
 BwdShape bwd_shape(const ss_bwd_args *a) {
     BwdShape s;
     const int64_t rows = a->batch * a->dim;
-    int64_t k = rows / (16 * 2 * kNumSMs);
-    s.kgroups = (int)(k < 1 ? 1 : (k > 8 ? 8 : k));
+    // K channel groups of kBwdChannelsPerGroup per CTA; at least ~4 waves of 2 CTAs / SM.
+    const int cpg = kBwdChannelsPerGroup;
+    int64_t k = rows / (cpg * 2 * kNumSMs * 4);
+    s.kgroups = (int)(k < 1 ? 1 : (k > kBwdMaxGroups ? kBwdMaxGroups : k));
     const int64_t dpg = a->n_groups > 0 ? a->dim / a->n_groups : a->dim;
-    s.tiles_per_group = (int)((dpg + 16 * s.kgroups - 1) / (16 * s.kgroups));
+    s.tiles_per_group = (int)((dpg + cpg * s.kgroups - 1) / (cpg * s.kgroups));
     s.lpitch = round_up(a->seqlen, 4);
     s.acc_bytes = round_up(a->batch * a->n_groups * a->dstate * s.lpitch * 4, 256);
-    s.dh_bytes = round_up(rows * 16 * 4, 256);
+    s.dh_bytes = 0;
     return s;
 }
 
@@ -227,7 +229,6 @@ int ss_bwd(const ss_bwd_args *a, void *stream) {
     char *ws = reinterpret_cast<char *>(a->workspace);
     float *acc_dB = reinterpret_cast<float *>(ws);
     float *acc_dC = reinterpret_cast<float *>(ws + s.acc_bytes);
-    float *ws_dh = reinterpret_cast<float *>(ws + 2 * s.acc_bytes);
     if ((e = cudaMemsetAsync(ws, 0, 2 * s.acc_bytes, st)) != cudaSuccess) return cuda_fail(e, "ss_bwd memset acc");
 
     BwdParams p{};
@@ -249,7 +250,7 @@ int ss_bwd(const ss_bwd_args *a, void *stream) {
     p.du_bs = a->du_bs; p.du_ds = a->du_ds; p.ddelta_bs = a->ddelta_bs; p.ddelta_ds = a->ddelta_ds;
     p.dz_bs = a->dz_bs; p.dz_ds = a->dz_ds; p.out_z_bs = a->out_z_bs; p.out_z_ds = a->out_z_ds;
     p.dA = a->dA; p.dD = a->dD; p.ddelta_bias = a->ddelta_bias;
-    p.acc_dB = acc_dB; p.acc_dC = acc_dC; p.ws_dh = ws_dh;
+    p.acc_dB = acc_dB; p.acc_dC = acc_dC;
     bool aligned = al16(a->u) && al16(a->delta) && al16(a->B) && al16(a->C) && al16(a->dout) &&
                    al16(a->du) && al16(a->ddelta) && st16(a->u_bs, es) && st16(a->u_ds, es) &&
                    st16(a->delta_bs, es) && st16(a->delta_ds, es) && st16(a->B_bs, es) && st16(a->B_gs, es) &&

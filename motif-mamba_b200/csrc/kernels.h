@@ -42,14 +42,14 @@ struct BwdParams {
     int64_t du_bs, du_ds, ddelta_bs, ddelta_ds, dz_bs, dz_ds, out_z_bs, out_z_ds;
     float *dA, *dD, *ddelta_bias;
     float *acc_dB, *acc_dC;  // fp32 accumulators (batch, n_groups, dstate, lpitch)
-    float *ws_dh;            // reverse-recurrence carry between chunks (batch, dim, 16)
 };
 
 int fwd_state_pad(int dstate);
 int fwd_channels_per_cta(int dstate);
 cudaError_t launch_ss_fwd(const FwdParams &p, int itype, bool has_z, cudaStream_t st);
 
-constexpr int kBwdChannelsPerGroup = 16;  // channel lanes per CTA pass (256 threads / 16 states)
+constexpr int kBwdChannelsPerGroup = 8;  // channels (warps) per CTA pass of the backward
+constexpr int kBwdMaxGroups = 8;         // channel groups per backward CTA
 cudaError_t launch_ss_bwd(const BwdParams &p, int itype, bool has_z, cudaStream_t st);
 cudaError_t launch_conv1d_fwd(const conv1d_args &a, bool vec, cudaStream_t st);
 cudaError_t launch_conv1d_bwd(const conv1d_args &a, bool vec, cudaStream_t st);

@@ -10,366 +10,364 @@
 //   dD    += doutg_t u_t              ddelta_bias += ddelta_t
 //   dz     = dout * out * sigma(z) (1 + z (1 - sigma(z))),   doutg = dout * silu(z)
 //
-// Design (B200): a CTA of 256 threads covers 16 channels x 16 states per pass; thread
-// (cl, n) owns state n of channel cl and walks the sequence serially, so every
-// recurrence is a register FMA chain.  The forward's chunk states x (one every 256
-// steps) seed each chunk; a forward pre-pass over the chunk stores the state at every
-// 16-step tile start in shared memory, then the tiles are processed in reverse: the
-// 16-step forward is recomputed into registers (decay a_t and state h_t), then the
-// reverse recurrence runs over them.  Per-element work (softplus, z gate, du, ddelta,
-// dz) is done once per element by "element threads" (one per (t, channel) of the tile);
-// the sums over states (sum_n dh B, sum_n A dh p) go through a padded shared-memory
-// transpose.  dB / dC are first summed over the CTA's channels on chip (warp shuffle +
-// shared memory) into a per-chunk fp32 accumulator that also sums the CTA's K channel
-// groups, and leave as one vector red.global.add.v4.f32 per 4 timesteps per chunk, so
-// the global atomic traffic is 1/(16 K) of a per-channel scheme.
+// Design (B200).  One warp owns one channel for one 256-step chunk: lane l owns the 8
+// consecutive timesteps 8l..8l+7, so every per-element quantity (softplus, z gate, du,
+// ddelta, dz) lives in the owning lane's registers, is loaded and stored with 16-byte
+// vector accesses, and the sums over states (sum_n dh B, sum_n A dh p) are in-register
+// FMA accumulations across the state loop.  For each state n the forward state is
+// rebuilt from the chunk state that ss_fwd stored in x (one every 256 steps): each lane
+// folds its 8 steps sequentially, a 5-level warp scan of (decay, state) pairs gives each
+// lane its incoming state, and the 8 steps are replayed; the reverse recurrence is the
+// mirror image (local fold, reverse warp scan, replay), seeded by the carry from the
+// later chunk.  A CTA runs 8 warps on 8 channels of one batch row at a time and K such
+// channel groups per chunk: dB / dC (sums over channels) are reduced over the 8 warps
+// through shared memory into a per-chunk fp32 accumulator that also sums the K groups,
+// and leave once per chunk as vector red.global.add.v4.f32, 1/(8K) of the traffic of a
+// per-channel scheme.  B / C of the chunk are staged once per CTA and chunk, converted
+// to fp32 in a bank-conflict-free lane-interleaved layout.
 #include "common.cuh"
 #include "kernels.h"
 
 namespace mss {
 
 namespace bwd {
-constexpr int NT = 256;   // threads per CTA
-constexpr int NSP = 16;   // state lanes per channel (dstate <= 16, zero padded)
-constexpr int CL = 16;    // channels per pass
-constexpr int SEG = 16;   // timesteps per tile
-constexpr int FP = 20;    // padded row pitch (floats) of the fp32 per-tile arrays
-constexpr int XP = 36;    // padded row pitch (floats) of the (S1, S2) transpose rows
-constexpr int TILES_PER_CHUNK = kChunkLen / SEG;
+constexpr int W = 8;              // warps (channels) per CTA pass
+constexpr int NT = W * 32;        // threads per CTA
+constexpr int IT = 8;             // timesteps per lane
+constexpr int CK = kChunkLen;     // timesteps per chunk (= 32 lanes x IT)
+constexpr int NS = 16;            // states per thread loop (dstate <= 16)
+constexpr int KMAX = 8;           // channel groups per CTA
+static_assert(CK == 32 * IT, "a warp covers one chunk");
 }  // namespace bwd
 
-template <typename T, bool HAS_Z>
-struct BwdLayout {
-    static constexpr int RP = bwd::SEG * (int)sizeof(T) + 16;
-    static constexpr int NARR = HAS_Z ? 5 : 3;  // u, delta, dout, (z, out)
-    static constexpr int U_OFF = 0, DT_OFF = 16 * RP, DO_OFF = 32 * RP, Z_OFF = 48 * RP, OUT_OFF = 64 * RP;
-    static constexpr int B_OFF = NARR * 16 * RP, C_OFF = B_OFF + 16 * RP;
-    static constexpr int BUF = (NARR * 16 + 32) * RP;
-    static constexpr int F_OFF = 2 * BUF;                                // DTF, DTU, DOG [16][FP]
-    static constexpr int BCF_OFF = F_OFF + 3 * 16 * bwd::FP * 4;         // B, C fp32 [2][16][FP]
-    static constexpr int XCH_OFF = BCF_OFF + 2 * 16 * bwd::FP * 4;       // (S1,S2) transpose | dB/dC partials
-    static constexpr int XCH_BYTES = 256 * bwd::XP * 4;                  // >= 8*2*16*16*4
-    static constexpr int ACC_OFF = XCH_OFF + XCH_BYTES;                  // [2][16][256] fp32
-    static constexpr int CK_OFF = ACC_OFF + 2 * 16 * kChunkLen * 4;      // [16 tiles][256] fp32
-    static constexpr int PB_OFF = CK_OFF + bwd::TILES_PER_CHUNK * bwd::NT * 4;  // [2][16 t][16 cl]
-    static constexpr int SMEM = PB_OFF + 2 * 16 * 16 * 4;
+// Lane-interleaved chunk layout: timestep t = 8 l + 4 h + j (lane l, half h, j < 4) lives at
+// h * 128 + 4 l + j, so each lane reads its 8 steps as two conflict-free 16-byte loads.
+struct BwdSmem {
+    float BC[2][bwd::NS][bwd::CK];            // B, C of the chunk, fp32
+    float RED[2][bwd::W][2][bwd::CK];         // double-buffered per-state dB / dC partials
+    float ACC[2][bwd::NS][bwd::CK];           // chunk accumulator of dB / dC
+    float DHC[bwd::KMAX][bwd::W][bwd::NS];    // reverse-recurrence carry into the previous chunk
+    float DAACC[bwd::KMAX][bwd::W][bwd::NS];  // dA accumulators
+    float PBD[bwd::KMAX][bwd::W][2];          // dD, ddelta_bias accumulators
 };
+
+template <typename T>
+__device__ __forceinline__ void load_items(const T *row, int64_t t0, int64_t L, bool vec, float (&v)[8]) {
+    if (vec && t0 + 8 <= L) {
+        Vec8<T>::load(row + t0, v);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = (t0 + i < L) ? to_f<T>(row[t0 + i]) : 0.f;
+    }
+}
+template <typename T>
+__device__ __forceinline__ void store_items(T *row, int64_t t0, int64_t L, bool vec, const float (&v)[8]) {
+    if (vec && t0 + 8 <= L) {
+        Vec8<T>::store(row + t0, v);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            if (t0 + i < L) row[t0 + i] = from_f<T>(v[i]);
+    }
+}
+__device__ __forceinline__ void ld8(const float *base, int lane, float (&v)[8]) {
+    const float4 a = *reinterpret_cast<const float4 *>(base + lane * 4);
+    const float4 c = *reinterpret_cast<const float4 *>(base + 128 + lane * 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
+}
+__device__ __forceinline__ void st8(float *base, int lane, const float (&v)[8]) {
+    *reinterpret_cast<float4 *>(base + lane * 4) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4 *>(base + 128 + lane * 4) = make_float4(v[4], v[5], v[6], v[7]);
+}
 
 template <typename T, bool HAS_Z>
 __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
     using namespace bwd;
-    using Ly = BwdLayout<T, HAS_Z>;
-    constexpr int RP = Ly::RP;
-    extern __shared__ __align__(16) char smem[];
-    float *DTF = reinterpret_cast<float *>(smem + Ly::F_OFF);
-    float *DTU = DTF + 16 * FP;
-    float *DOG = DTU + 16 * FP;
-    float *BF = reinterpret_cast<float *>(smem + Ly::BCF_OFF);
-    float *CF = BF + 16 * FP;
-    float *XCH = reinterpret_cast<float *>(smem + Ly::XCH_OFF);
-    float *ACC = reinterpret_cast<float *>(smem + Ly::ACC_OFF);
-    float *CKPT = reinterpret_cast<float *>(smem + Ly::CK_OFF);
-    float *PB = reinterpret_cast<float *>(smem + Ly::PB_OFF);
+    extern __shared__ __align__(16) char smem_raw[];
+    BwdSmem &S = *reinterpret_cast<BwdSmem *>(smem_raw);
+    const unsigned FULL = 0xffffffffu;
 
-    const int tid = threadIdx.x;
-    // state-thread coordinates
-    const int s_cl = tid >> 4, s_n = tid & 15;
-    // element-thread coordinates (prologue / epilogue): t-major so a warp holds 2 timesteps
-    const int e_t = tid >> 4, e_cl = tid & 15;
-
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const int g = blockIdx.x / p.tiles_per_group;
     const int tile = blockIdx.x - g * p.tiles_per_group;
     const int b = blockIdx.y;
     const int64_t L = p.seqlen;
-    const bool aligned = p.aligned != 0;
+    const bool vec = p.aligned != 0;
+    const int K = p.kgroups;
 
-    for (int i = tid; i < 2 * 16 * kChunkLen; i += NT) ACC[i] = 0.f;
+    for (int i = tid; i < 2 * NS * CK; i += NT) (&S.ACC[0][0][0])[i] = 0.f;
+    for (int i = tid; i < KMAX * W * NS; i += NT) {
+        (&S.DHC[0][0][0])[i] = 0.f;
+        (&S.DAACC[0][0][0])[i] = 0.f;
+    }
+    for (int i = tid; i < KMAX * W * 2; i += NT) (&S.PBD[0][0][0])[i] = 0.f;
 
     const T *gB = reinterpret_cast<const T *>(p.B) + (int64_t)b * p.B_bs + (int64_t)g * p.B_gs;
     const T *gC = reinterpret_cast<const T *>(p.C) + (int64_t)b * p.C_bs + (int64_t)g * p.C_gs;
 
     for (int k = p.n_chunks - 1; k >= 0; --k) {
-        const int64_t kt0 = (int64_t)k * kChunkLen;
-        const int clen = (int)min((int64_t)kChunkLen, L - kt0);
-        const int ntile = (clen + SEG - 1) / SEG;
-        for (int cgi = 0; cgi < p.kgroups; ++cgi) {
-            const int cbase = (tile * p.kgroups + cgi) * CL;  // within the group
-            const int nvalid = min(CL, p.dpg - cbase);
-            if (nvalid <= 0) break;  // uniform over the CTA
-            const int c0 = g * p.dpg + cbase;
-
-            // per-state-thread constants
-            const bool s_vch = s_cl < nvalid;
-            const int s_d = c0 + (s_vch ? s_cl : 0);
-            const bool s_vst = s_vch && s_n < p.dstate;
-            const float An = s_vst ? p.A[(int64_t)s_d * p.A_ds + (int64_t)s_n * p.A_ns] : 0.f;
-            const float A2 = An * kLog2e;
-            const int64_t s_row = (int64_t)b * p.dim + s_d;
-            // per-element-thread constants
-            const bool e_vch = e_cl < nvalid;
-            const int e_d = c0 + (e_vch ? e_cl : 0);
-            const float bias = (p.delta_bias && e_vch) ? p.delta_bias[(int64_t)e_d * p.delta_bias_s] : 0.f;
-            const float Dv = (p.D && e_vch) ? p.D[(int64_t)e_d * p.D_s] : 0.f;
-
-            const T *gu = reinterpret_cast<const T *>(p.u) + (int64_t)b * p.u_bs + (int64_t)c0 * p.u_ds;
-            const T *gdt = reinterpret_cast<const T *>(p.delta) + (int64_t)b * p.delta_bs + (int64_t)c0 * p.delta_ds;
-            const T *gdo = reinterpret_cast<const T *>(p.dout) + (int64_t)b * p.dout_bs + (int64_t)c0 * p.dout_ds;
-            const T *gz = HAS_Z ? reinterpret_cast<const T *>(p.z) + (int64_t)b * p.z_bs + (int64_t)c0 * p.z_ds : nullptr;
-            const T *gout = HAS_Z ? reinterpret_cast<const T *>(p.out) + (int64_t)b * p.out_bs + (int64_t)c0 * p.out_ds : nullptr;
-
-            auto stage = [&](int buf, int j, bool full) {
-                char *rb = smem + buf * Ly::BUF;
-                const int64_t t0 = kt0 + (int64_t)j * SEG;
-                const int tv = (int)min((int64_t)SEG, L - t0);
-                stage_tile<T, SEG>(rb + Ly::U_OFF, RP, gu, p.u_ds, 16, nvalid, t0, tv, aligned, tid, NT);
-                stage_tile<T, SEG>(rb + Ly::DT_OFF, RP, gdt, p.delta_ds, 16, nvalid, t0, tv, aligned, tid, NT);
-                stage_tile<T, SEG>(rb + Ly::B_OFF, RP, gB, p.B_ns, 16, p.dstate, t0, tv, aligned, tid, NT);
-                if (full) {
-                    stage_tile<T, SEG>(rb + Ly::DO_OFF, RP, gdo, p.dout_ds, 16, nvalid, t0, tv, aligned, tid, NT);
-                    stage_tile<T, SEG>(rb + Ly::C_OFF, RP, gC, p.C_ns, 16, p.dstate, t0, tv, aligned, tid, NT);
-                    if constexpr (HAS_Z) {
-                        stage_tile<T, SEG>(rb + Ly::Z_OFF, RP, gz, p.z_ds, 16, nvalid, t0, tv, aligned, tid, NT);
-                        stage_tile<T, SEG>(rb + Ly::OUT_OFF, RP, gout, p.out_ds, 16, nvalid, t0, tv, aligned, tid, NT);
-                    }
-                }
-            };
-            auto elem = [&](const char *rb, int off) -> float {
-                return to_f<T>(reinterpret_cast<const T *>(rb + off + e_cl * RP)[e_t]);
-            };
-
-            // ---------------- forward pre-pass over the chunk: tile-start checkpoints -------------
-            float h = 0.f;
-            if (k > 0 && s_vst) h = p.x[(s_row * p.n_chunks + (k - 1)) * 2 * p.dstate + 2 * s_n + 1];
-            stage(0, 0, false);
-            cp_async_commit();
-            for (int j = 0; j < ntile; ++j) {
-                if (j + 1 < ntile) {
-                    stage((j + 1) & 1, j + 1, false);
-                    cp_async_commit();
-                    cp_async_wait<1>();
-                } else {
-                    cp_async_wait<0>();
-                }
-                __syncthreads();
-                {
-                    const char *rb = smem + (j & 1) * Ly::BUF;
-                    const bool vt = kt0 + j * SEG + e_t < L;
-                    float dv = elem(rb, Ly::DT_OFF) + bias;
-                    if (p.softplus) dv = softplus20(dv);
-                    dv = vt ? dv : 0.f;
-                    DTF[e_cl * FP + e_t] = dv;
-                    DTU[e_cl * FP + e_t] = dv * elem(rb, Ly::U_OFF);
-                    // B tile to fp32 [n][t] (thread -> (n = tid>>4, t = tid&15))
-                    BF[(tid >> 4) * FP + (tid & 15)] =
-                        to_f<T>(reinterpret_cast<const T *>(rb + Ly::B_OFF + (tid >> 4) * RP)[tid & 15]);
-                }
-                __syncthreads();
-                CKPT[j * NT + tid] = h;
+        const int64_t kt0 = (int64_t)k * CK;
+        __syncthreads();  // previous chunk's accumulator flush and B/C reads are done
+        // ---- stage B, C of this chunk (fp32; zero beyond dstate / seqlen)
+        for (int i = tid; i < 2 * NS * 32; i += NT) {
+            const int q = i / (NS * 32), rem = i - q * NS * 32, n = rem >> 5, l = rem & 31;
+            float v[8];
+            if (n < p.dstate) {
+                const T *row = (q == 0 ? gB + (int64_t)n * p.B_ns : gC + (int64_t)n * p.C_ns);
+                load_items(row, kt0 + l * 8, L, vec, v);
+            } else {
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const float4 f = *reinterpret_cast<const float4 *>(DTF + s_cl * FP + 4 * q);
-                    const float4 w = *reinterpret_cast<const float4 *>(DTU + s_cl * FP + 4 * q);
-                    const float4 bb = *reinterpret_cast<const float4 *>(BF + s_n * FP + 4 * q);
-                    h = fmaf(ex2(f.x * A2), h, w.x * bb.x);
-                    h = fmaf(ex2(f.y * A2), h, w.y * bb.y);
-                    h = fmaf(ex2(f.z * A2), h, w.z * bb.z);
-                    h = fmaf(ex2(f.w * A2), h, w.w * bb.w);
-                }
+                for (int j = 0; j < 8; ++j) v[j] = 0.f;
             }
-            __syncthreads();
-
-            // ---------------- reverse pass over the chunk's tiles ----------------------------------
-            float carry = (k < p.n_chunks - 1 && s_vch) ? p.ws_dh[s_row * NSP + s_n] : 0.f;
-            float dA_acc = 0.f, dD_part = 0.f, db_part = 0.f;
-            stage(0, ntile - 1, true);
-            cp_async_commit();
-            for (int it = 0; it < ntile; ++it) {
-                const int j = ntile - 1 - it;
-                const int64_t t0 = kt0 + (int64_t)j * SEG;
-                const int tv = (int)min((int64_t)SEG, L - t0);
-                if (j > 0) {
-                    stage((it + 1) & 1, j - 1, true);
-                    cp_async_commit();
-                    cp_async_wait<1>();
-                } else {
-                    cp_async_wait<0>();
-                }
-                __syncthreads();
-                char *rb = smem + (it & 1) * Ly::BUF;
-                // -- prologue: one thread per (t, channel) element
-                const bool vt = e_t < tv;
-                const float uf = elem(rb, Ly::U_OFF);
-                const float dtv = elem(rb, Ly::DT_OFF) + bias;
-                float dtf = p.softplus ? softplus20(dtv) : dtv;
-                const float dgate = (p.softplus && dtv <= 20.f) ? sigmoidf_(dtv) : 1.f;
-                dtf = vt ? dtf : 0.f;
-                const float dout = vt ? elem(rb, Ly::DO_OFF) : 0.f;
-                float doutg = dout, dzv = 0.f, outz = 0.f;
-                if constexpr (HAS_Z) {
-                    const float zv = elem(rb, Ly::Z_OFF);
-                    const float ov = elem(rb, Ly::OUT_OFF);
-                    const float sz = sigmoidf_(zv);
-                    const float silu = zv * sz;
-                    doutg = dout * silu;
-                    dzv = dout * ov * sz * (1.f + zv * (1.f - sz));
-                    outz = ov * silu;
-                }
-                DTF[e_cl * FP + e_t] = dtf;
-                DTU[e_cl * FP + e_t] = dtf * uf;
-                DOG[e_cl * FP + e_t] = doutg;
-                BF[(tid >> 4) * FP + (tid & 15)] =
-                    to_f<T>(reinterpret_cast<const T *>(rb + Ly::B_OFF + (tid >> 4) * RP)[tid & 15]);
-                CF[(tid >> 4) * FP + (tid & 15)] =
-                    to_f<T>(reinterpret_cast<const T *>(rb + Ly::C_OFF + (tid >> 4) * RP)[tid & 15]);
-                __syncthreads();
-
-                // -- state threads: recompute the tile forward, then the reverse recurrence
-                float a[SEG], hs[SEG];
-                {
-                    float hh = CKPT[j * NT + tid];
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const float4 f = *reinterpret_cast<const float4 *>(DTF + s_cl * FP + 4 * q);
-                        const float4 w = *reinterpret_cast<const float4 *>(DTU + s_cl * FP + 4 * q);
-                        const float4 bb = *reinterpret_cast<const float4 *>(BF + s_n * FP + 4 * q);
-                        const float fv[4] = {f.x, f.y, f.z, f.w}, wv[4] = {w.x, w.y, w.z, w.w};
-                        const float bv[4] = {bb.x, bb.y, bb.z, bb.w};
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            a[4 * q + i] = ex2(fv[i] * A2);
-                            hh = fmaf(a[4 * q + i], hh, wv[i] * bv[i]);
-                            hs[4 * q + i] = hh;
-                        }
-                    }
-                }
-                float dBv[SEG], dCv[SEG];
-#pragma unroll
-                for (int q = 3; q >= 0; --q) {
-                    const float4 f = *reinterpret_cast<const float4 *>(DTF + s_cl * FP + 4 * q);
-                    const float4 w = *reinterpret_cast<const float4 *>(DTU + s_cl * FP + 4 * q);
-                    const float4 o = *reinterpret_cast<const float4 *>(DOG + s_cl * FP + 4 * q);
-                    const float4 bb = *reinterpret_cast<const float4 *>(BF + s_n * FP + 4 * q);
-                    const float4 cc = *reinterpret_cast<const float4 *>(CF + s_n * FP + 4 * q);
-                    const float fv[4] = {f.x, f.y, f.z, f.w}, wv[4] = {w.x, w.y, w.z, w.w};
-                    const float ov[4] = {o.x, o.y, o.z, o.w}, bv[4] = {bb.x, bb.y, bb.z, bb.w};
-                    const float cv[4] = {cc.x, cc.y, cc.z, cc.w};
-#pragma unroll
-                    for (int i = 3; i >= 0; --i) {
-                        const int t = 4 * q + i;
-                        const float dh = fmaf(ov[i], cv[i], carry);
-                        carry = a[t] * dh;
-                        const float pv = fmaf(-wv[i], bv[i], hs[t]);  // a_t * h_{t-1}
-                        const float gv = dh * pv;
-                        dA_acc = fmaf(fv[i], gv, dA_acc);
-                        *reinterpret_cast<float2 *>(XCH + (t * 16 + s_cl) * XP + 2 * s_n) =
-                            make_float2(dh * bv[i], An * gv);
-                        dBv[t] = dh * wv[i];
-                        dCv[t] = ov[i] * hs[t];
-                    }
-                }
-                __syncthreads();
-
-                // -- epilogue: element threads reduce (S1, S2) over states and form du, ddelta
-                {
-                    const float4 *xr = reinterpret_cast<const float4 *>(XCH + (e_t * 16 + e_cl) * XP);
-                    float S1 = 0.f, S2 = 0.f;
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) {
-                        const float4 v = xr[q];
-                        S1 += v.x + v.z;
-                        S2 += v.y + v.w;
-                    }
-                    const float du = fmaf(dtf, S1, Dv * doutg);
-                    const float ddelta = fmaf(uf, S1, S2) * dgate;
-                    if (vt && e_vch) {
-                        dD_part = fmaf(doutg, uf, dD_part);
-                        db_part += ddelta;
-                    }
-                    reinterpret_cast<T *>(rb + Ly::U_OFF + e_cl * RP)[e_t] = from_f<T>(du);
-                    reinterpret_cast<T *>(rb + Ly::DT_OFF + e_cl * RP)[e_t] = from_f<T>(ddelta);
-                    if constexpr (HAS_Z) {
-                        reinterpret_cast<T *>(rb + Ly::Z_OFF + e_cl * RP)[e_t] = from_f<T>(dzv);
-                        reinterpret_cast<T *>(rb + Ly::OUT_OFF + e_cl * RP)[e_t] = from_f<T>(outz);
-                    }
-                }
-                __syncthreads();
-
-                // -- dB / dC: sum the warp's two channels, then park per-warp partials
-#pragma unroll
-                for (int t = 0; t < SEG; ++t) {
-                    dBv[t] += __shfl_xor_sync(0xffffffffu, dBv[t], 16);
-                    dCv[t] += __shfl_xor_sync(0xffffffffu, dCv[t], 16);
-                }
-                if ((s_cl & 1) == 0) {
-                    float *rbB = XCH + ((s_cl >> 1) * 2 + 0) * 256 + s_n * 16;
-                    float *rbC = XCH + ((s_cl >> 1) * 2 + 1) * 256 + s_n * 16;
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        reinterpret_cast<float4 *>(rbB)[q] = make_float4(dBv[4 * q], dBv[4 * q + 1], dBv[4 * q + 2], dBv[4 * q + 3]);
-                        reinterpret_cast<float4 *>(rbC)[q] = make_float4(dCv[4 * q], dCv[4 * q + 1], dCv[4 * q + 2], dCv[4 * q + 3]);
-                    }
-                }
-                {
-                    T *gdu = reinterpret_cast<T *>(p.du) + (int64_t)b * p.du_bs + (int64_t)c0 * p.du_ds;
-                    T *gdd = reinterpret_cast<T *>(p.ddelta) + (int64_t)b * p.ddelta_bs + (int64_t)c0 * p.ddelta_ds;
-                    store_tile<T, SEG>(gdu, p.du_ds, rb + Ly::U_OFF, RP, nvalid, t0, tv, aligned, tid, NT);
-                    store_tile<T, SEG>(gdd, p.ddelta_ds, rb + Ly::DT_OFF, RP, nvalid, t0, tv, aligned, tid, NT);
-                    if constexpr (HAS_Z) {
-                        T *gdz = reinterpret_cast<T *>(p.dz) + (int64_t)b * p.dz_bs + (int64_t)c0 * p.dz_ds;
-                        store_tile<T, SEG>(gdz, p.dz_ds, rb + Ly::Z_OFF, RP, nvalid, t0, tv, aligned, tid, NT);
-                        if (p.recompute_out_z) {
-                            T *goz = reinterpret_cast<T *>(p.out_z) + (int64_t)b * p.out_z_bs + (int64_t)c0 * p.out_z_ds;
-                            store_tile<T, SEG>(goz, p.out_z_ds, rb + Ly::OUT_OFF, RP, nvalid, t0, tv, aligned, tid, NT);
-                        }
-                    }
-                }
-                __syncthreads();
-                {   // thread (n, t): sum the 8 warps' partials into the chunk accumulator
-                    const int rn = tid >> 4, rt = tid & 15;
-                    float sb = 0.f, sc = 0.f;
-#pragma unroll
-                    for (int w = 0; w < 8; ++w) {
-                        sb += XCH[(w * 2 + 0) * 256 + rn * 16 + rt];
-                        sc += XCH[(w * 2 + 1) * 256 + rn * 16 + rt];
-                    }
-                    ACC[rn * kChunkLen + j * SEG + rt] += sb;
-                    ACC[16 * kChunkLen + rn * kChunkLen + j * SEG + rt] += sc;
-                }
-            }
-            // -- end of the (chunk, channel group) pass
-            if (s_vch) {
-                p.ws_dh[s_row * NSP + s_n] = carry;
-                if (s_vst) atomicAdd(p.dA + (int64_t)s_d * p.dstate + s_n, dA_acc);
-            }
-            PB[e_t * 16 + e_cl] = dD_part;
-            PB[256 + e_t * 16 + e_cl] = db_part;
-            __syncthreads();
-            if (tid < 32) {
-                const int q = tid >> 4, cl = tid & 15;
-                float sum = 0.f;
-#pragma unroll
-                for (int t = 0; t < 16; ++t) sum += PB[q * 256 + t * 16 + cl];
-                if (cl < nvalid) {
-                    float *dst = q == 0 ? p.dD : p.ddelta_bias;
-                    if (dst) atomicAdd(dst + c0 + cl, sum);
-                }
-            }
-            __syncthreads();
-        }
-        // -- flush the chunk's dB / dC (summed over this CTA's channels) to global
-        for (int i = tid; i < 2 * 16 * (kChunkLen / 4); i += NT) {
-            const int q = i / (16 * (kChunkLen / 4));
-            const int rem = i - q * 16 * (kChunkLen / 4);
-            const int n = rem / (kChunkLen / 4), t4 = (rem - n * (kChunkLen / 4)) * 4;
-            float *src = ACC + q * 16 * kChunkLen + n * kChunkLen + t4;
-            if (n < p.dstate && t4 < clen) {
-                float *dst = (q == 0 ? p.acc_dB : p.acc_dC) +
-                             (((int64_t)b * p.n_groups + g) * p.dstate + n) * p.lpitch + kt0 + t4;
-                red_add_v4(dst, src[0], src[1], src[2], src[3]);
-            }
-            src[0] = 0.f; src[1] = 0.f; src[2] = 0.f; src[3] = 0.f;
+            st8(&S.BC[q][n][0], l, v);
         }
         __syncthreads();
+
+        for (int cg = 0; cg < K; ++cg) {
+            const int cin = (tile * K + cg) * W + w;  // channel within the group
+            const bool valid = cin < p.dpg;
+            const int d = g * p.dpg + (valid ? cin : 0);
+            const int64_t row = (int64_t)b * p.dim + d;
+            const int64_t t0 = kt0 + lane * IT;
+
+            // ---- per-element prologue (this lane's 8 steps)
+            float uf[8], dtf[8], dtu[8], dog[8];
+            {
+                float dv[8], dov[8];
+                load_items(reinterpret_cast<const T *>(p.u) + (int64_t)b * p.u_bs + (int64_t)d * p.u_ds, t0, L,
+                           vec, uf);
+                load_items(reinterpret_cast<const T *>(p.delta) + (int64_t)b * p.delta_bs + (int64_t)d * p.delta_ds,
+                           t0, L, vec, dv);
+                load_items(reinterpret_cast<const T *>(p.dout) + (int64_t)b * p.dout_bs + (int64_t)d * p.dout_ds,
+                           t0, L, vec, dov);
+                const float bias = p.delta_bias ? p.delta_bias[(int64_t)d * p.delta_bias_s] : 0.f;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    float x = dv[i] + bias;
+                    if (p.softplus) x = softplus20(x);
+                    dtf[i] = (valid && t0 + i < L) ? x : 0.f;
+                    dtu[i] = dtf[i] * uf[i];
+                    dog[i] = valid ? dov[i] : 0.f;
+                }
+                if constexpr (HAS_Z) {
+                    float zv[8], ov[8], dzv[8], ozv[8];
+                    load_items(reinterpret_cast<const T *>(p.z) + (int64_t)b * p.z_bs + (int64_t)d * p.z_ds, t0, L,
+                               vec, zv);
+                    load_items(reinterpret_cast<const T *>(p.out) + (int64_t)b * p.out_bs + (int64_t)d * p.out_ds,
+                               t0, L, vec, ov);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const float sz = sigmoidf_(zv[i]);
+                        const float silu = zv[i] * sz;
+                        dzv[i] = dog[i] * ov[i] * sz * (1.f + zv[i] * (1.f - sz));
+                        ozv[i] = ov[i] * silu;
+                        dog[i] *= silu;
+                    }
+                    if (valid) {
+                        store_items(reinterpret_cast<T *>(p.dz) + (int64_t)b * p.dz_bs + (int64_t)d * p.dz_ds, t0, L,
+                                    vec, dzv);
+                        if (p.recompute_out_z)
+                            store_items(reinterpret_cast<T *>(p.out_z) + (int64_t)b * p.out_z_bs +
+                                            (int64_t)d * p.out_z_ds, t0, L, vec, ozv);
+                    }
+                }
+            }
+            float sdt = 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) sdt += dtf[i];
+
+            float S1[8], S2[8], dAl[NS];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) S1[i] = S2[i] = 0.f;
+
+#pragma unroll
+            for (int n = 0; n < NS; ++n) {
+                dAl[n] = 0.f;
+                if (n >= p.dstate) continue;  // uniform over the CTA
+                const float An = valid ? p.A[(int64_t)d * p.A_ds + (int64_t)n * p.A_ns] : 0.f;
+                const float A2 = An * kLog2e;
+                float Bv[8], a[8], h[8];
+                ld8(&S.BC[0][n][0], lane, Bv);
+                // forward: local fold, warp scan of (decay, state), replay
+                float H = 0.f;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    a[i] = ex2(dtf[i] * A2);
+                    h[i] = dtu[i] * Bv[i];  // b_i, replaced by the state below
+                    H = fmaf(a[i], H, h[i]);
+                }
+                const float Pl = ex2(A2 * sdt);  // decay over the lane's 8 steps
+                float Ad = Pl, Hd = H;
+#pragma unroll
+                for (int off = 1; off < 32; off <<= 1) {
+                    const float Ap = __shfl_up_sync(FULL, Ad, off), Hp = __shfl_up_sync(FULL, Hd, off);
+                    if (lane >= off) {
+                        Hd = fmaf(Ad, Hp, Hd);
+                        Ad *= Ap;
+                    }
+                }
+                const float h_chunk =
+                    (k > 0 && valid) ? p.x[(row * p.n_chunks + (k - 1)) * 2 * p.dstate + 2 * n + 1] : 0.f;
+                float h_in;
+                {
+                    const float Ae = __shfl_up_sync(FULL, Ad, 1), He = __shfl_up_sync(FULL, Hd, 1);
+                    h_in = lane == 0 ? h_chunk : fmaf(Ae, h_chunk, He);
+                }
+                float hp = h_in;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    h[i] = fmaf(a[i], hp, h[i]);
+                    hp = h[i];
+                }
+                // reverse: local fold of dh (without the carry), reverse warp scan, replay
+                float Cv[8];
+                ld8(&S.BC[1][n][0], lane, Cv);
+                float Dl = 0.f;
+#pragma unroll
+                for (int i = 7; i >= 0; --i) {
+                    Cv[i] *= dog[i];  // e_i = doutg_i C_i
+                    Dl = fmaf(i < 7 ? a[i + 1] : 0.f, Dl, Cv[i]);
+                }
+                float Pd = Pl, Qd = a[0] * Dl;  // lane aggregate: passes Q + P * carry_in to the left
+#pragma unroll
+                for (int off = 1; off < 32; off <<= 1) {
+                    const float Pr = __shfl_down_sync(FULL, Pd, off), Qr = __shfl_down_sync(FULL, Qd, off);
+                    if (lane + off < 32) {
+                        Qd = fmaf(Pd, Qr, Qd);
+                        Pd *= Pr;
+                    }
+                }
+                const float c_chunk = S.DHC[cg][w][n];
+                float carry;
+                {
+                    const float Pe = __shfl_down_sync(FULL, Pd, 1), Qe = __shfl_down_sync(FULL, Qd, 1);
+                    carry = lane == 31 ? c_chunk : fmaf(Pe, c_chunk, Qe);
+                }
+                float dAp = 0.f;
+#pragma unroll
+                for (int i = 7; i >= 0; --i) {
+                    const float dh = Cv[i] + carry;
+                    carry = a[i] * dh;
+                    const float pv = a[i] * (i > 0 ? h[i - 1] : h_in);  // a_t h_{t-1}
+                    const float gv = dh * pv;
+                    S1[i] = fmaf(dh, Bv[i], S1[i]);
+                    S2[i] = fmaf(An, gv, S2[i]);
+                    dAp = fmaf(dtf[i], gv, dAp);
+                    Cv[i] = dh;
+                }
+                if (lane == 0) S.DHC[cg][w][n] = carry;  // carry into the previous chunk
+                dAl[n] = dAp;
+                // dB / dC partials of this warp's channel -> reduce over the CTA's warps
+                {
+                    float dBv[8], dCv[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        dBv[i] = Cv[i] * dtu[i];
+                        dCv[i] = dog[i] * h[i];
+                    }
+                    st8(&S.RED[n & 1][w][0][0], lane, dBv);
+                    st8(&S.RED[n & 1][w][1][0], lane, dCv);
+                }
+                __syncthreads();
+                {
+                    const int q = tid >> 7, pp = (tid & 127) * 2;
+                    float2 s = make_float2(0.f, 0.f);
+#pragma unroll
+                    for (int ww = 0; ww < W; ++ww) {
+                        const float2 v = *reinterpret_cast<const float2 *>(&S.RED[n & 1][ww][q][pp]);
+                        s.x += v.x;
+                        s.y += v.y;
+                    }
+                    float2 *acc = reinterpret_cast<float2 *>(&S.ACC[q][n][pp]);
+                    float2 cur = *acc;
+                    cur.x += s.x;
+                    cur.y += s.y;
+                    *acc = cur;
+                }
+            }
+            // ---- per-element epilogue
+            {
+                const float Dv = p.D ? p.D[(int64_t)d * p.D_s] : 0.f;
+                float du[8], dd[8], dv[8], dDp = 0.f, dbp = 0.f;
+                load_items(reinterpret_cast<const T *>(p.delta) + (int64_t)b * p.delta_bs + (int64_t)d * p.delta_ds,
+                           t0, L, vec, dv);
+                const float bias = p.delta_bias ? p.delta_bias[(int64_t)d * p.delta_bias_s] : 0.f;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float x = dv[i] + bias;
+                    const float gate = (p.softplus && x <= 20.f) ? sigmoidf_(x) : 1.f;
+                    du[i] = fmaf(dtf[i], S1[i], Dv * dog[i]);
+                    dd[i] = fmaf(uf[i], S1[i], S2[i]) * gate;
+                    if (t0 + i < L) {
+                        dDp = fmaf(dog[i], uf[i], dDp);
+                        dbp += dd[i];
+                    }
+                }
+                if (valid) {
+                    store_items(reinterpret_cast<T *>(p.du) + (int64_t)b * p.du_bs + (int64_t)d * p.du_ds, t0, L,
+                                vec, du);
+                    store_items(reinterpret_cast<T *>(p.ddelta) + (int64_t)b * p.ddelta_bs + (int64_t)d * p.ddelta_ds,
+                                t0, L, vec, dd);
+                }
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) {
+                    dDp += __shfl_xor_sync(FULL, dDp, off);
+                    dbp += __shfl_xor_sync(FULL, dbp, off);
+                }
+                if (lane == 0) {
+                    S.PBD[cg][w][0] += dDp;
+                    S.PBD[cg][w][1] += dbp;
+                }
+            }
+            // ---- dA of this pass: sum the lanes' per-state partials through the idle RED buffer
+            __syncthreads();
+            {
+                float *scr = &S.RED[0][0][0][0] + w * 512;  // 32 lanes x 16 states
+#pragma unroll
+                for (int q4 = 0; q4 < NS / 4; ++q4)
+                    *reinterpret_cast<float4 *>(scr + lane * 16 + 4 * q4) =
+                        make_float4(dAl[4 * q4], dAl[4 * q4 + 1], dAl[4 * q4 + 2], dAl[4 * q4 + 3]);
+                __syncwarp();
+                if (lane < NS) {
+                    float s = 0.f;
+#pragma unroll 8
+                    for (int j = 0; j < 32; ++j) s += scr[j * 16 + lane];
+                    S.DAACC[cg][w][lane] += s;
+                }
+            }
+            __syncthreads();
+        }
+        // ---- flush the chunk's dB / dC (summed over this CTA's channels)
+        __syncthreads();
+        const int clen = (int)min((int64_t)CK, L - kt0);
+        for (int i = tid; i < 2 * NS * (CK / 4); i += NT) {
+            const int q = i / (NS * (CK / 4)), rem = i - q * NS * (CK / 4);
+            const int n = rem / (CK / 4), pos = (rem - n * (CK / 4)) * 4;
+            const int t = ((pos >> 2) & 31) * 8 + (pos >> 7) * 4;  // first timestep of this 4-group
+            float *src = &S.ACC[q][n][pos];
+            if (n < p.dstate && t < clen) {
+                float *dst = (q == 0 ? p.acc_dB : p.acc_dC) +
+                             (((int64_t)b * p.n_groups + g) * p.dstate + n) * p.lpitch + kt0 + t;
+                red_add_v4(dst, src[0], src[1], src[2], src[3]);
+            }
+            src[0] = src[1] = src[2] = src[3] = 0.f;
+        }
+    }
+    __syncthreads();
+    for (int i = tid; i < K * W * NS; i += NT) {
+        const int cg = i / (W * NS), rem = i - cg * W * NS, ww = rem / NS, n = rem - ww * NS;
+        const int cin = (tile * K + cg) * W + ww;
+        if (cin < p.dpg && n < p.dstate)
+            atomicAdd(p.dA + (int64_t)(g * p.dpg + cin) * p.dstate + n, S.DAACC[cg][ww][n]);
+    }
+    for (int i = tid; i < K * W; i += NT) {
+        const int cg = i / W, ww = i - cg * W;
+        const int cin = (tile * K + cg) * W + ww;
+        if (cin < p.dpg) {
+            if (p.dD) atomicAdd(p.dD + g * p.dpg + cin, S.PBD[cg][ww][0]);
+            if (p.ddelta_bias) atomicAdd(p.ddelta_bias + g * p.dpg + cin, S.PBD[cg][ww][1]);
+        }
     }
 }
 
@@ -401,16 +399,16 @@ cudaError_t launch_acc_to_out(const float *acc, int64_t lpitch, void *out, int i
 
 template <typename T, bool HAS_Z>
 static cudaError_t launch_bwd_t(const BwdParams &p, cudaStream_t st) {
-    using Ly = BwdLayout<T, HAS_Z>;
     auto kern = ss_bwd_kernel<T, HAS_Z>;
+    constexpr int SMEM = (int)sizeof(BwdSmem);
     static bool configured = false;
     if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Ly::SMEM);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
         if (e != cudaSuccess) return e;
         configured = true;
     }
     dim3 grid(p.tiles_per_group * p.n_groups, p.batch);
-    kern<<<grid, bwd::NT, Ly::SMEM, st>>>(p);
+    kern<<<grid, bwd::NT, SMEM, st>>>(p);
     return cudaGetLastError();
 }
 
