@@ -162,6 +162,21 @@ MSS_API int ss_bwd_workspace_size(const ss_bwd_args *a, int64_t *bytes);
 MSS_API int ss_fwd(const ss_fwd_args *a, void *stream);
 /* selective scan backward: writes du, ddelta, dA, dB, dC, dD, ddelta_bias, dz, out_z.  (selective_scan.cpp:415-618) */
 MSS_API int ss_bwd(const ss_bwd_args *a, void *stream);
+/* Scratch bytes ss_bwd_noalloc owns per GPU (64 MiB: enough for batch x n_groups x dstate
+ * x seqlen up to 8 Mi, e.g. 32 x 1 x 16 x 16384). */
+#define MSS_BWD_NOALLOC_SCRATCH_BYTES (64ll << 20)
+
+/* ss_bwd for callers that cannot allocate device memory: code whose device memory is owned
+ * by another allocator (a framework's caching pool it may not bypass), or a host runtime
+ * that forbids cudaMalloc in its steady state because cudaMalloc can synchronize the device
+ * and has no latency bound.  No counterpart in the reference.  Same arguments and results as ss_bwd,
+ * but `workspace` / `workspace_bytes` are ignored: the scratch is a static device array of
+ * MSS_BWD_NOALLOC_SCRATCH_BYTES that this library keeps on every GPU it is loaded on.
+ * Sizes needing more scratch than that fail with MSS_ERR_WORKSPACE.  The first call on a
+ * device looks the array's address up (make it before any stream capture); every call shares
+ * the array, so calls that overlap on the GPU race.  It calls no allocator. */
+MSS_API int ss_bwd_noalloc(const ss_bwd_args *a, void *stream);
+
 /* depthwise causal conv1d (+SiLU) forward / backward (causal-conv1d API) */
 MSS_API int conv1d_fwd(const conv1d_args *a, void *stream);
 MSS_API int conv1d_bwd(const conv1d_args *a, void *stream);

@@ -128,6 +128,10 @@ BwdShape bwd_shape(const ss_bwd_args *a) {
 
 }  // namespace
 
+namespace mss {
+int set_last_error(int code, const char *msg) { return fail(code, "%s", msg); }
+}  // namespace mss
+
 extern "C" {
 
 int32_t ss_chunk_len(void) { return kChunkLen; }

@@ -44,6 +44,9 @@ struct BwdParams {
     float *acc_dB, *acc_dC;  // fp32 accumulators (batch, n_groups, dstate, lpitch)
 };
 
+// Sets the text ss_last_error() reports on this thread and returns `code`.
+int set_last_error(int code, const char *msg);
+
 int fwd_state_pad(int dstate);
 int fwd_channels_per_cta(int dstate);
 cudaError_t launch_ss_fwd(const FwdParams &p, int itype, bool has_z, cudaStream_t st);

@@ -115,6 +115,7 @@ SYMBOLS = [
     ("ss_bwd_workspace_size", [ctypes.POINTER(SsBwdArgs), ctypes.POINTER(i64)], ctypes.c_int),
     ("ss_fwd", [ctypes.POINTER(SsFwdArgs), vp], ctypes.c_int),
     ("ss_bwd", [ctypes.POINTER(SsBwdArgs), vp], ctypes.c_int),
+    ("ss_bwd_noalloc", [ctypes.POINTER(SsBwdArgs), vp], ctypes.c_int),
     ("conv1d_fwd", [ctypes.POINTER(Conv1dArgs), vp], ctypes.c_int),
     ("conv1d_bwd", [ctypes.POINTER(Conv1dArgs), vp], ctypes.c_int),
     ("conv1d_update", [ctypes.POINTER(Conv1dUpdateArgs), vp], ctypes.c_int),
