@@ -97,9 +97,53 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 // softplus with torch's threshold of 20 (the reference kernel uses the same rule,
-// selective_scan_fwd_kernel.cuh:388-390).
-__device__ __forceinline__ float softplus20(float x) { return x <= 20.f ? log1pf(__expf(x)) : x; }
-__device__ __forceinline__ float sigmoidf_(float x) { return 1.f / (1.f + __expf(-x)); }
+// selective_scan_fwd_kernel.cuh:388-390): log(1 + e^x) for x <= 20, x above.
+// log(1 + y), y = e^x, is taken from the SFU logarithm where the result is >= ~0.06; for
+// smaller y the SFU log of (1 + y) would lose relative accuracy (its error is absolute), so
+// the Taylor series y - y^2/2 + y^3/3 - y^4/4 + y^5/5 is used (truncation < y^6/6, i.e.
+// < 1e-8 relative for y < 1/16).
+__device__ __forceinline__ float softplus20(float x) {
+    const float y = __expf(x);
+    const float big = __logf(1.f + y);
+    const float small = y * fmaf(y, fmaf(y, fmaf(y, fmaf(y, 0.2f, -0.25f), 1.f / 3.f), -0.5f), 1.f);
+    const float r = y < 0.0625f ? small : big;
+    return x <= 20.f ? r : x;
+}
+// 1 / (1 + e^-x) with the SFU exponential and a fast reciprocal (relative error ~1e-7).
+__device__ __forceinline__ float sigmoidf_(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
+
+// ---- packed fp32 pairs (Blackwell fma/mul .f32x2: one instruction for two lanes of math) ----
+typedef unsigned long long f32x2;
+__device__ __forceinline__ f32x2 pack2(float lo, float hi) {
+    f32x2 r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ float2 unpack2(f32x2 v) {
+    float2 r;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+    return r;
+}
+__device__ __forceinline__ f32x2 fma2(f32x2 a, f32x2 b, f32x2 c) {
+    f32x2 d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ f32x2 mul2(f32x2 a, f32x2 b) {
+    f32x2 d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ f32x2 add2(f32x2 a, f32x2 b) {
+    f32x2 d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+// 2^x of both halves (two SFU ex2).
+__device__ __forceinline__ f32x2 ex2x2(f32x2 x) {
+    const float2 v = unpack2(x);
+    return pack2(ex2(v.x), ex2(v.y));
+}
 
 // ---- cp.async (16-byte, zero-filling) ---------------------------------------------------
 // Copies src_bytes (0..16) from global to shared and zero-fills the rest of the 16 bytes.

@@ -177,14 +177,12 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
 #pragma unroll
             for (int i = 0; i < 8; ++i) sdt += dtf[i];
 
-            float S1[8], S2[8], dAl[NS];
+            float S1[8], S2[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) S1[i] = S2[i] = 0.f;
 
-#pragma unroll
-            for (int n = 0; n < NS; ++n) {
-                dAl[n] = 0.f;
-                if (n >= p.dstate) continue;  // uniform over the CTA
+#pragma unroll 1
+            for (int n = 0; n < p.dstate; ++n) {  // uniform over the CTA
                 const float An = valid ? p.A[(int64_t)d * p.A_ds + (int64_t)n * p.A_ns] : 0.f;
                 const float A2 = An * kLog2e;
                 float Bv[8], a[8], h[8];
@@ -256,8 +254,12 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
                     dAp = fmaf(dtf[i], gv, dAp);
                     Cv[i] = dh;
                 }
-                if (lane == 0) S.DHC[cg][w][n] = carry;  // carry into the previous chunk
-                dAl[n] = dAp;
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) dAp += __shfl_xor_sync(FULL, dAp, off);
+                if (lane == 0) {
+                    S.DHC[cg][w][n] = carry;  // carry into the previous chunk
+                    S.DAACC[cg][w][n] += dAp;
+                }
                 // dB / dC partials of this warp's channel -> reduce over the CTA's warps
                 {
                     float dBv[8], dCv[8];
@@ -318,22 +320,6 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
                 if (lane == 0) {
                     S.PBD[cg][w][0] += dDp;
                     S.PBD[cg][w][1] += dbp;
-                }
-            }
-            // ---- dA of this pass: sum the lanes' per-state partials through the idle RED buffer
-            __syncthreads();
-            {
-                float *scr = &S.RED[0][0][0][0] + w * 512;  // 32 lanes x 16 states
-#pragma unroll
-                for (int q4 = 0; q4 < NS / 4; ++q4)
-                    *reinterpret_cast<float4 *>(scr + lane * 16 + 4 * q4) =
-                        make_float4(dAl[4 * q4], dAl[4 * q4 + 1], dAl[4 * q4 + 2], dAl[4 * q4 + 3]);
-                __syncwarp();
-                if (lane < NS) {
-                    float s = 0.f;
-#pragma unroll 8
-                    for (int j = 0; j < 32; ++j) s += scr[j * 16 + lane];
-                    S.DAACC[cg][w][lane] += s;
                 }
             }
             __syncthreads();

@@ -13,8 +13,9 @@
 // in-thread FMA chain.  A CTA owns CH consecutive channels of one (batch, group); tiles
 // of TT timesteps of u / delta / z (rows of the CTA's channels) and of B / C (rows of the
 // group's states, shared by all CH channels) are staged into shared memory with 16-byte
-// cp.async, double-buffered so the next tile streams in while the current one is
-// computed.  B/C are converted to fp32 once per tile into a [t][n] layout that every
+// cp.async into a single buffer (six co-resident CTAs per SM hide each other's load
+// latency; the small footprint is what lets config 4 run as one wave).  The states are
+// updated in pairs with Blackwell's packed fma/mul.f32x2.  B/C are converted to fp32 once per tile into a [t][n] layout that every
 // thread reads with broadcast 16-byte loads.  Outputs are written in place into the
 // staged u / z rows and leave through coalesced 16-byte stores.
 //
@@ -29,8 +30,8 @@ namespace mss {
 
 template <int NS> struct FwdCfg {
     static constexpr int CH = NS <= 16 ? 128 : 64;  // channels (threads) per CTA
-    static constexpr int TT = 32;                   // timesteps per staged tile
-    static constexpr int MINB = NS <= 16 ? 4 : 1;
+    static constexpr int TT = 16;                   // timesteps per staged tile
+    static constexpr int MINB = NS <= 16 ? 6 : 1;  // 6 x 128 threads: one wave at config 4
 };
 
 template <typename T, int NS, bool HAS_Z, bool CARRY>
@@ -45,7 +46,7 @@ struct FwdLayout {
     static constexpr int BCW = NS * NST_ARR;  // floats per timestep in the fp32 B/C tile
     static constexpr int U_OFF = 0, DT_OFF = CH * RP, Z_OFF = 2 * CH * RP;
     static constexpr int B_OFF = CH * NCH_ARR * RP, C_OFF = B_OFF + NS * RP;
-    static constexpr int SMEM = 2 * BUF + TT * BCW * 4;
+    static constexpr int SMEM = BUF + TT * BCW * 4;  // single-buffered: co-resident CTAs hide the loads
 };
 
 template <typename T, int NS, bool HAS_Z, bool CARRY>
@@ -53,7 +54,7 @@ __global__ void __launch_bounds__(FwdCfg<NS>::CH, FwdCfg<NS>::MINB) ss_fwd_kerne
     using Ly = FwdLayout<T, NS, HAS_Z, CARRY>;
     constexpr int CH = Ly::CH, TT = Ly::TT, RP = Ly::RP, BCW = Ly::BCW;
     extern __shared__ __align__(16) char smem[];
-    float *bc = reinterpret_cast<float *>(smem + 2 * Ly::BUF);
+    float *bc = reinterpret_cast<float *>(smem + Ly::BUF);
 
     const int tid = threadIdx.x;
     const int g = blockIdx.x / p.tiles_per_group;
@@ -77,9 +78,14 @@ __global__ void __launch_bounds__(FwdCfg<NS>::CH, FwdCfg<NS>::MINB) ss_fwd_kerne
     const float Dv = (p.D != nullptr && valid) ? p.D[(int64_t)d * p.D_s] : 0.f;
     const float bias = (p.delta_bias != nullptr && valid) ? p.delta_bias[(int64_t)d * p.delta_bias_s] : 0.f;
 
-    float h[NS];
+    // State and decay rates as packed pairs (states 2m, 2m+1).
+    constexpr int NP = NS / 2;
+    f32x2 h2[NP], A2p[NP];
 #pragma unroll
-    for (int n = 0; n < NS; ++n) h[n] = 0.f;
+    for (int m = 0; m < NP; ++m) {
+        h2[m] = pack2(0.f, 0.f);
+        A2p[m] = pack2(A2[2 * m], A2[2 * m + 1]);
+    }
     float cum = 0.f;  // sum of dt since t = 0 (main pass) or since the segment start (carry pass)
     const int64_t row = (int64_t)b * p.dim + d;
     if (!CARRY && s > 0 && valid) {
@@ -87,7 +93,10 @@ __global__ void __launch_bounds__(FwdCfg<NS>::CH, FwdCfg<NS>::MINB) ss_fwd_kerne
             const float dts = p.ws_dts[row * p.n_seg + sp];
             const float *H = p.ws_h + (row * p.n_seg + sp) * NS;
 #pragma unroll
-            for (int n = 0; n < NS; ++n) h[n] = fmaf(ex2(A2[n] * dts), h[n], H[n]);
+            for (int m = 0; m < NP; ++m) {
+                const float2 hv = unpack2(h2[m]);
+                h2[m] = pack2(fmaf(ex2(A2[2 * m] * dts), hv.x, H[2 * m]), fmaf(ex2(A2[2 * m + 1] * dts), hv.y, H[2 * m + 1]));
+            }
             cum += dts;
         }
     }
@@ -111,20 +120,14 @@ __global__ void __launch_bounds__(FwdCfg<NS>::CH, FwdCfg<NS>::MINB) ss_fwd_kerne
     };
 
     const int ntiles = (int)((t_end - t_begin + TT - 1) / TT);
-    if (ntiles > 0) stage(0, t_begin);
-    cp_async_commit();
     for (int it = 0; it < ntiles; ++it) {
         const int64_t t0 = t_begin + (int64_t)it * TT;
         const int tv = (int)min((int64_t)TT, t_end - t0);
-        if (it + 1 < ntiles) {
-            stage((it + 1) & 1, t0 + TT);
-            cp_async_commit();
-            cp_async_wait<1>();
-        } else {
-            cp_async_wait<0>();
-        }
+        stage(0, t0);
+        cp_async_commit();
+        cp_async_wait<0>();
         __syncthreads();
-        char *rb = smem + (it & 1) * Ly::BUF;
+        char *rb = smem;
         // B / C tile -> fp32 [t][n] (C after B), once per CTA.
         for (int i = tid; i < TT * NS; i += CH) {
             const int n = i % NS, t = i / NS;
@@ -153,29 +156,17 @@ __global__ void __launch_bounds__(FwdCfg<NS>::CH, FwdCfg<NS>::MINB) ss_fwd_kerne
             float y[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                const float4 *bcr = reinterpret_cast<const float4 *>(bc + (g8 + j) * BCW);
-                float acc = 0.f;
+                const f32x2 *bcr = reinterpret_cast<const f32x2 *>(bc + (g8 + j) * BCW);
+                const f32x2 dt2 = pack2(dv[j], dv[j]), du2 = pack2(dtu[j], dtu[j]);
+                f32x2 acc2[2] = {pack2(0.f, 0.f), pack2(0.f, 0.f)};  // two chains of pair sums
 #pragma unroll
-                for (int q = 0; q < NS / 4; ++q) {
-                    const float4 bb = bcr[q];
-                    const float bv[4] = {bb.x, bb.y, bb.z, bb.w};
-                    if constexpr (CARRY) {
-#pragma unroll
-                        for (int k = 0; k < 4; ++k) {
-                            const int n = 4 * q + k;
-                            h[n] = fmaf(ex2(dv[j] * A2[n]), h[n], dtu[j] * bv[k]);
-                        }
-                    } else {
-                        const float4 cc = bcr[NS / 4 + q];
-                        const float cv[4] = {cc.x, cc.y, cc.z, cc.w};
-#pragma unroll
-                        for (int k = 0; k < 4; ++k) {
-                            const int n = 4 * q + k;
-                            h[n] = fmaf(ex2(dv[j] * A2[n]), h[n], dtu[j] * bv[k]);
-                            acc = fmaf(cv[k], h[n], acc);
-                        }
-                    }
+                for (int m = 0; m < NP; ++m) {
+                    const f32x2 a2 = ex2x2(mul2(dt2, A2p[m]));
+                    h2[m] = fma2(a2, h2[m], mul2(du2, bcr[m]));
+                    if constexpr (!CARRY) acc2[m & 1] = fma2(bcr[NP + m], h2[m], acc2[m & 1]);
                 }
+                const float2 accv = unpack2(add2(acc2[0], acc2[1]));
+                const float acc = accv.x + accv.y;
                 y[j] = acc;
             }
             if constexpr (!CARRY) {
@@ -202,7 +193,8 @@ __global__ void __launch_bounds__(FwdCfg<NS>::CH, FwdCfg<NS>::MINB) ss_fwd_kerne
                 for (int n = 0; n < NS; ++n)
                     if (n < p.dstate) {
                         xr[2 * n] = ex2(A2[n] * cum);
-                        xr[2 * n + 1] = h[n];
+                        const float2 hv = unpack2(h2[n >> 1]);
+                        xr[2 * n + 1] = (n & 1) ? hv.y : hv.x;
                     }
             }
             __syncthreads();
@@ -218,7 +210,11 @@ __global__ void __launch_bounds__(FwdCfg<NS>::CH, FwdCfg<NS>::MINB) ss_fwd_kerne
     if (CARRY && valid) {
         float *H = p.ws_h + (row * p.n_seg + s) * NS;
 #pragma unroll
-        for (int n = 0; n < NS; ++n) H[n] = h[n];
+        for (int m = 0; m < NP; ++m) {
+            const float2 hv = unpack2(h2[m]);
+            H[2 * m] = hv.x;
+            H[2 * m + 1] = hv.y;
+        }
         p.ws_dts[row * p.n_seg + s] = cum;
     }
 }

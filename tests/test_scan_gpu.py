@@ -195,3 +195,13 @@ def test_bwd_accepts_preallocated_dz_in_place():
     assert res[7].data_ptr() == dz_view.data_ptr()
     assert (buf[:, :16] == 7.0).all()
     assert_close(res[8], out_z, 1e-5, 1e-5, "recomputed out_z")
+
+
+def test_scan_extreme_delta_and_z():
+    """delta + bias spanning the softplus threshold (-30 .. 30) and large |z| (sigmoid tails)."""
+    inp, dout = make_scan_inputs(2, 32, 200, 16, torch.float32, seed=9)
+    inp["delta"] = inp["delta"] * 12.0
+    inp["z"] = inp["z"] * 15.0
+    ref_out, ref_last, ref_grads = oracle(inp, dout, True)
+    out, last, grads = run_kernel(inp, dout, True)
+    compare(out, last, grads, ref_out, ref_last, ref_grads, torch.float32, "extreme delta/z")
