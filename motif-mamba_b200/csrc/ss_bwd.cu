@@ -25,6 +25,8 @@
 // and leave once per chunk as vector red.global.add.v4.f32, 1/(8K) of the traffic of a
 // per-channel scheme.  B / C of the chunk are staged once per CTA and chunk, converted
 // to fp32 in a bank-conflict-free lane-interleaved layout.
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -42,13 +44,19 @@ static_assert(CK == 32 * IT, "a warp covers one chunk");
 
 // Lane-interleaved chunk layout: timestep t = 8 l + 4 h + j (lane l, half h, j < 4) lives at
 // h * 128 + 4 l + j, so each lane reads its 8 steps as two conflict-free 16-byte loads.
-struct BwdSmem {
-    float BC[2][bwd::NS][bwd::CK];            // B, C of the chunk, fp32
+// 16-bit inputs keep B / C in their own type here (converted when read), which leaves room
+// for the per-warp prefetch buffers of the next pass's per-step inputs.
+template <typename T> struct BwdSmemT {
+    static constexpr bool kPrefetch = sizeof(T) == 2;
+    using BCT = typename std::conditional<kPrefetch, T, float>::type;
+    BCT BC[2][bwd::NS][bwd::CK];              // B, C of the chunk
     float RED[2][bwd::W][2][bwd::CK];         // double-buffered per-state dB / dC partials
     float ACC[2][bwd::NS][bwd::CK];           // chunk accumulator of dB / dC
     float DHC[bwd::KMAX][bwd::W][bwd::NS];    // reverse-recurrence carry into the previous chunk
     float DAACC[bwd::KMAX][bwd::W][bwd::NS];  // dA accumulators
     float PBD[bwd::KMAX][bwd::W][2];          // dD, ddelta_bias accumulators
+    float AX[bwd::W][2][bwd::NS];             // this pass's A row and chunk-start states, per warp
+    T PF[kPrefetch ? bwd::W : 1][5][bwd::CK]; // next pass's u, delta, dout, z, out (lane slices)
 };
 
 template <typename T>
@@ -76,6 +84,30 @@ __device__ __forceinline__ void ld8(const float *base, int lane, float (&v)[8]) 
     v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
     v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
 }
+template <typename T> __device__ __forceinline__ void bc_ld8(const T *base, int lane, float (&v)[8]) {
+    // 16-bit layout: 4 values at [4 lane, 4 lane + 4) and 4 at [128 + 4 lane, ...)
+    const uint2 a = *reinterpret_cast<const uint2 *>(base + lane * 4);
+    const uint2 c = *reinterpret_cast<const uint2 *>(base + 128 + lane * 4);
+    const T *pa = reinterpret_cast<const T *>(&a), *pc = reinterpret_cast<const T *>(&c);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        v[j] = to_f<T>(pa[j]);
+        v[4 + j] = to_f<T>(pc[j]);
+    }
+}
+template <> __device__ __forceinline__ void bc_ld8<float>(const float *base, int lane, float (&v)[8]) {
+    ld8(base, lane, v);
+}
+template <typename T> __device__ __forceinline__ void bc_st8(T *base, int lane, const float (&v)[8]) {
+    T a[4], c[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        a[j] = from_f<T>(v[j]);
+        c[j] = from_f<T>(v[4 + j]);
+    }
+    *reinterpret_cast<uint2 *>(base + lane * 4) = *reinterpret_cast<const uint2 *>(a);
+    *reinterpret_cast<uint2 *>(base + 128 + lane * 4) = *reinterpret_cast<const uint2 *>(c);
+}
 __device__ __forceinline__ void st8(float *base, int lane, const float (&v)[8]) {
     *reinterpret_cast<float4 *>(base + lane * 4) = make_float4(v[0], v[1], v[2], v[3]);
     *reinterpret_cast<float4 *>(base + 128 + lane * 4) = make_float4(v[4], v[5], v[6], v[7]);
@@ -85,7 +117,8 @@ template <typename T, bool HAS_Z>
 __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
     using namespace bwd;
     extern __shared__ __align__(16) char smem_raw[];
-    BwdSmem &S = *reinterpret_cast<BwdSmem *>(smem_raw);
+    using Smem = BwdSmemT<T>;
+    Smem &S = *reinterpret_cast<Smem *>(smem_raw);
     const unsigned FULL = 0xffffffffu;
 
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
@@ -106,6 +139,30 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
     const T *gB = reinterpret_cast<const T *>(p.B) + (int64_t)b * p.B_bs + (int64_t)g * p.B_gs;
     const T *gC = reinterpret_cast<const T *>(p.C) + (int64_t)b * p.C_bs + (int64_t)g * p.C_gs;
 
+    // Per-step inputs of a pass: each lane copies its own 8 steps of u, delta, dout (z, out)
+    // for the NEXT pass into its warp's slice of S.PF while the current pass computes.
+    const bool pf = Smem::kPrefetch && vec;
+    const T *arr_base[5] = {reinterpret_cast<const T *>(p.u) + (int64_t)b * p.u_bs,
+                            reinterpret_cast<const T *>(p.delta) + (int64_t)b * p.delta_bs,
+                            reinterpret_cast<const T *>(p.dout) + (int64_t)b * p.dout_bs,
+                            HAS_Z ? reinterpret_cast<const T *>(p.z) + (int64_t)b * p.z_bs : nullptr,
+                            HAS_Z ? reinterpret_cast<const T *>(p.out) + (int64_t)b * p.out_bs : nullptr};
+    const int64_t arr_ds[5] = {p.u_ds, p.delta_ds, p.dout_ds, p.z_ds, p.out_ds};
+    constexpr int NARR = HAS_Z ? 5 : 3;
+    auto prefetch = [&](int kk, int cgg) {
+        const int cin = (tile * K + cgg) * W + w;
+        const int dd = g * p.dpg + (cin < p.dpg ? cin : 0);
+        const int64_t tt = (int64_t)kk * CK + lane * IT;
+        const int nb = (int)max((int64_t)0, min((int64_t)IT, L - tt)) * (int)sizeof(T);
+#pragma unroll
+        for (int a = 0; a < NARR; ++a) {
+            const T *src = arr_base[a] + (int64_t)dd * arr_ds[a] + (nb > 0 ? tt : 0);
+            cp_async16(&S.PF[Smem::kPrefetch ? w : 0][a][lane * IT], src, nb);
+        }
+        cp_async_commit();
+    };
+    if (pf && p.n_chunks > 0) prefetch(p.n_chunks - 1, 0);
+
     for (int k = p.n_chunks - 1; k >= 0; --k) {
         const int64_t kt0 = (int64_t)k * CK;
         __syncthreads();  // previous chunk's accumulator flush and B/C reads are done
@@ -120,7 +177,7 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
 #pragma unroll
                 for (int j = 0; j < 8; ++j) v[j] = 0.f;
             }
-            st8(&S.BC[q][n][0], l, v);
+            if constexpr (Smem::kPrefetch) bc_st8(&S.BC[q][n][0], l, v); else st8(&S.BC[q][n][0], l, v);
         }
         __syncthreads();
 
@@ -131,31 +188,44 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
             const int64_t row = (int64_t)b * p.dim + d;
             const int64_t t0 = kt0 + lane * IT;
 
-            // ---- per-element prologue (this lane's 8 steps)
-            float uf[8], dtf[8], dtu[8], dog[8];
+            // ---- per-element prologue (this lane's 8 steps).  Per-step arrays are held as
+            // packed pairs (steps 2m, 2m+1) so independent per-step math issues as f32x2.
+            f32x2 uf2[4], dtf2[4], dtu2[4], dog2[4];
             {
-                float dv[8], dov[8];
-                load_items(reinterpret_cast<const T *>(p.u) + (int64_t)b * p.u_bs + (int64_t)d * p.u_ds, t0, L,
-                           vec, uf);
-                load_items(reinterpret_cast<const T *>(p.delta) + (int64_t)b * p.delta_bs + (int64_t)d * p.delta_ds,
-                           t0, L, vec, dv);
-                load_items(reinterpret_cast<const T *>(p.dout) + (int64_t)b * p.dout_bs + (int64_t)d * p.dout_ds,
-                           t0, L, vec, dov);
+                float uf[8], dv[8], dov[8], zv[8], ov[8];
+                if (pf) {
+                    cp_async_wait<0>();
+                    const T *pw = &S.PF[Smem::kPrefetch ? w : 0][0][lane * IT];
+                    Vec8<T>::load(pw, uf);
+                    Vec8<T>::load(pw + CK, dv);
+                    Vec8<T>::load(pw + 2 * CK, dov);
+                    if constexpr (HAS_Z) {
+                        Vec8<T>::load(pw + 3 * CK, zv);
+                        Vec8<T>::load(pw + 4 * CK, ov);
+                    }
+                    __syncwarp();
+                    if (cg + 1 < K) prefetch(k, cg + 1);
+                    else if (k > 0) prefetch(k - 1, 0);
+                } else {
+                    load_items(arr_base[0] + (int64_t)d * p.u_ds, t0, L, vec, uf);
+                    load_items(arr_base[1] + (int64_t)d * p.delta_ds, t0, L, vec, dv);
+                    load_items(arr_base[2] + (int64_t)d * p.dout_ds, t0, L, vec, dov);
+                    if constexpr (HAS_Z) {
+                        load_items(arr_base[3] + (int64_t)d * p.z_ds, t0, L, vec, zv);
+                        load_items(arr_base[4] + (int64_t)d * p.out_ds, t0, L, vec, ov);
+                    }
+                }
                 const float bias = p.delta_bias ? p.delta_bias[(int64_t)d * p.delta_bias_s] : 0.f;
+                float dtf[8], dog[8];
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
                     float x = dv[i] + bias;
                     if (p.softplus) x = softplus20(x);
                     dtf[i] = (valid && t0 + i < L) ? x : 0.f;
-                    dtu[i] = dtf[i] * uf[i];
                     dog[i] = valid ? dov[i] : 0.f;
                 }
                 if constexpr (HAS_Z) {
-                    float zv[8], ov[8], dzv[8], ozv[8];
-                    load_items(reinterpret_cast<const T *>(p.z) + (int64_t)b * p.z_bs + (int64_t)d * p.z_ds, t0, L,
-                               vec, zv);
-                    load_items(reinterpret_cast<const T *>(p.out) + (int64_t)b * p.out_bs + (int64_t)d * p.out_ds,
-                               t0, L, vec, ov);
+                    float dzv[8], ozv[8];
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
                         const float sz = sigmoidf_(zv[i]);
@@ -172,138 +242,228 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
                                             (int64_t)d * p.out_z_ds, t0, L, vec, ozv);
                     }
                 }
+#pragma unroll
+                for (int m = 0; m < 4; ++m) {
+                    uf2[m] = pack2(uf[2 * m], uf[2 * m + 1]);
+                    dtf2[m] = pack2(dtf[2 * m], dtf[2 * m + 1]);
+                    dog2[m] = pack2(dog[2 * m], dog[2 * m + 1]);
+                    dtu2[m] = mul2(dtf2[m], uf2[m]);
+                }
             }
-            float sdt = 0.f;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) sdt += dtf[i];
+            float sdt;
+            {
+                const float2 s = unpack2(add2(add2(dtf2[0], dtf2[1]), add2(dtf2[2], dtf2[3])));
+                sdt = s.x + s.y;
+            }
 
-            float S1[8], S2[8];
+            f32x2 S1[4], S2[4];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) S1[i] = S2[i] = 0.f;
+            for (int m = 0; m < 4; ++m) S1[m] = S2[m] = pack2(0.f, 0.f);
+            // A row and the chunk-start states of this channel, read once per pass (off the
+            // per-state dependency chain)
+            if (lane < p.dstate) {
+                S.AX[w][0][lane] = valid ? p.A[(int64_t)d * p.A_ds + (int64_t)lane * p.A_ns] : 0.f;
+                S.AX[w][1][lane] =
+                    (k > 0 && valid) ? p.x[(row * p.n_chunks + (k - 1)) * 2 * p.dstate + 2 * lane + 1] : 0.f;
+            }
+            __syncwarp();
 
+            // Two states per iteration, interleaved through every phase, so each warp always
+            // has two independent dependency chains in flight.  An odd dstate pads the last
+            // pair with a state whose A, B and C are zero (it contributes nothing).
 #pragma unroll 1
-            for (int n = 0; n < p.dstate; ++n) {  // uniform over the CTA
-                const float An = valid ? p.A[(int64_t)d * p.A_ds + (int64_t)n * p.A_ns] : 0.f;
-                const float A2 = An * kLog2e;
-                float Bv[8], a[8], h[8];
-                ld8(&S.BC[0][n][0], lane, Bv);
-                // forward: local fold, warp scan of (decay, state), replay
-                float H = 0.f;
+            for (int n0 = 0; n0 < p.dstate; n0 += 2) {  // uniform over the CTA
+                const bool has1 = n0 + 1 < p.dstate;
+                float An[2], A2[2], Pl[2];
+                f32x2 A2p[2], Anp[2];
+                f32x2 Bv[2][4], b2[2][4];
+                float a[2][8];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    a[i] = ex2(dtf[i] * A2);
-                    h[i] = dtu[i] * Bv[i];  // b_i, replaced by the state below
-                    H = fmaf(a[i], H, h[i]);
+                for (int s = 0; s < 2; ++s) {
+                    const int n = n0 + s;
+                    An[s] = (s == 0 || has1) ? S.AX[w][0][n] : 0.f;
+                    A2[s] = An[s] * kLog2e;
+                    A2p[s] = pack2(A2[s], A2[s]);
+                    Anp[s] = pack2(An[s], An[s]);
+                    float bv8[8];
+                    bc_ld8(&S.BC[0][s == 0 || has1 ? n : n0][0], lane, bv8);
+                    const float z = (s == 0 || has1) ? 1.f : 0.f;
+#pragma unroll
+                    for (int m = 0; m < 4; ++m) Bv[s][m] = pack2(z * bv8[2 * m], z * bv8[2 * m + 1]);
+#pragma unroll
+                    for (int m = 0; m < 4; ++m) {
+                        const float2 v = unpack2(ex2x2(mul2(dtf2[m], A2p[s])));
+                        a[s][2 * m] = v.x;
+                        a[s][2 * m + 1] = v.y;
+                        b2[s][m] = mul2(dtu2[m], Bv[s][m]);
+                    }
+                    Pl[s] = ex2(A2[s] * sdt);  // decay over the lane's 8 steps
                 }
-                const float Pl = ex2(A2 * sdt);  // decay over the lane's 8 steps
-                float Ad = Pl, Hd = H;
+                // local folds: forward state from zero, reverse dh without the carry
+                float H[2] = {0.f, 0.f}, Dl[2];
+                float e[2][8];
 #pragma unroll
-                for (int off = 1; off < 32; off <<= 1) {
-                    const float Ap = __shfl_up_sync(FULL, Ad, off), Hp = __shfl_up_sync(FULL, Hd, off);
-                    if (lane >= off) {
-                        Hd = fmaf(Ad, Hp, Hd);
-                        Ad *= Ap;
+                for (int s = 0; s < 2; ++s) {
+                    const int n = (s == 0 || has1) ? n0 + s : n0;
+                    float cv8[8];
+                    bc_ld8(&S.BC[1][n][0], lane, cv8);
+                    const float2 e0 = unpack2(mul2(dog2[0], pack2(cv8[0], cv8[1])));
+                    const float2 e1 = unpack2(mul2(dog2[1], pack2(cv8[2], cv8[3])));
+                    const float2 e2v = unpack2(mul2(dog2[2], pack2(cv8[4], cv8[5])));
+                    const float2 e3 = unpack2(mul2(dog2[3], pack2(cv8[6], cv8[7])));
+                    const float z = (s == 0 || has1) ? 1.f : 0.f;
+                    e[s][0] = z * e0.x; e[s][1] = z * e0.y; e[s][2] = z * e1.x; e[s][3] = z * e1.y;
+                    e[s][4] = z * e2v.x; e[s][5] = z * e2v.y; e[s][6] = z * e3.x; e[s][7] = z * e3.y;
+                }
+#pragma unroll
+                for (int m = 0; m < 4; ++m) {
+#pragma unroll
+                    for (int s = 0; s < 2; ++s) {
+                        const float2 bb = unpack2(b2[s][m]);
+                        H[s] = fmaf(a[s][2 * m], H[s], bb.x);
+                        H[s] = fmaf(a[s][2 * m + 1], H[s], bb.y);
                     }
                 }
-                const float h_chunk =
-                    (k > 0 && valid) ? p.x[(row * p.n_chunks + (k - 1)) * 2 * p.dstate + 2 * n + 1] : 0.f;
-                float h_in;
-                {
-                    const float Ae = __shfl_up_sync(FULL, Ad, 1), He = __shfl_up_sync(FULL, Hd, 1);
-                    h_in = lane == 0 ? h_chunk : fmaf(Ae, h_chunk, He);
-                }
-                float hp = h_in;
+                Dl[0] = e[0][7];
+                Dl[1] = e[1][7];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    h[i] = fmaf(a[i], hp, h[i]);
-                    hp = h[i];
+                for (int i = 6; i >= 0; --i) {
+                    Dl[0] = fmaf(a[0][i + 1], Dl[0], e[0][i]);
+                    Dl[1] = fmaf(a[1][i + 1], Dl[1], e[1][i]);
                 }
-                // reverse: local fold of dh (without the carry), reverse warp scan, replay
-                float Cv[8];
-                ld8(&S.BC[1][n][0], lane, Cv);
-                float Dl = 0.f;
+                // four independent warp scans, level by level: forward (decay, state) over the
+                // lanes below, reverse (decay, carry) over the lanes above, for both states
+                float Ad[2], Hd[2], Pd[2], Qd[2];
 #pragma unroll
-                for (int i = 7; i >= 0; --i) {
-                    Cv[i] *= dog[i];  // e_i = doutg_i C_i
-                    Dl = fmaf(i < 7 ? a[i + 1] : 0.f, Dl, Cv[i]);
+                for (int s = 0; s < 2; ++s) {
+                    Ad[s] = Pl[s]; Hd[s] = H[s]; Pd[s] = Pl[s]; Qd[s] = a[s][0] * Dl[s];
                 }
-                float Pd = Pl, Qd = a[0] * Dl;  // lane aggregate: passes Q + P * carry_in to the left
 #pragma unroll
                 for (int off = 1; off < 32; off <<= 1) {
-                    const float Pr = __shfl_down_sync(FULL, Pd, off), Qr = __shfl_down_sync(FULL, Qd, off);
-                    if (lane + off < 32) {
-                        Qd = fmaf(Pd, Qr, Qd);
-                        Pd *= Pr;
+                    float Ap[2], Hp[2], Pr[2], Qr[2];
+#pragma unroll
+                    for (int s = 0; s < 2; ++s) {
+                        Ap[s] = __shfl_up_sync(FULL, Ad[s], off);
+                        Hp[s] = __shfl_up_sync(FULL, Hd[s], off);
+                        Pr[s] = __shfl_down_sync(FULL, Pd[s], off);
+                        Qr[s] = __shfl_down_sync(FULL, Qd[s], off);
+                    }
+#pragma unroll
+                    for (int s = 0; s < 2; ++s) {
+                        if (lane >= off) {
+                            Hd[s] = fmaf(Ad[s], Hp[s], Hd[s]);
+                            Ad[s] *= Ap[s];
+                        }
+                        if (lane + off < 32) {
+                            Qd[s] = fmaf(Pd[s], Qr[s], Qd[s]);
+                            Pd[s] *= Pr[s];
+                        }
                     }
                 }
-                const float c_chunk = S.DHC[cg][w][n];
-                float carry;
+                float h_in[2], carry[2];
+#pragma unroll
+                for (int s = 0; s < 2; ++s) {
+                    const int n = (s == 0 || has1) ? n0 + s : n0;
+                    const float h_chunk = (s == 0 || has1) ? S.AX[w][1][n] : 0.f;
+                    const float c_chunk = (s == 0 || has1) ? S.DHC[cg][w][n] : 0.f;
+                    const float Ae = __shfl_up_sync(FULL, Ad[s], 1), He = __shfl_up_sync(FULL, Hd[s], 1);
+                    const float Pe = __shfl_down_sync(FULL, Pd[s], 1), Qe = __shfl_down_sync(FULL, Qd[s], 1);
+                    h_in[s] = lane == 0 ? h_chunk : fmaf(Ae, h_chunk, He);
+                    carry[s] = lane == 31 ? c_chunk : fmaf(Pe, c_chunk, Qe);
+                }
+                // replays: states forward, dh backward
+                f32x2 h2[2][4], dh2[2][4];
                 {
-                    const float Pe = __shfl_down_sync(FULL, Pd, 1), Qe = __shfl_down_sync(FULL, Qd, 1);
-                    carry = lane == 31 ? c_chunk : fmaf(Pe, c_chunk, Qe);
-                }
-                float dAp = 0.f;
+                    float hp[2] = {h_in[0], h_in[1]};
 #pragma unroll
-                for (int i = 7; i >= 0; --i) {
-                    const float dh = Cv[i] + carry;
-                    carry = a[i] * dh;
-                    const float pv = a[i] * (i > 0 ? h[i - 1] : h_in);  // a_t h_{t-1}
-                    const float gv = dh * pv;
-                    S1[i] = fmaf(dh, Bv[i], S1[i]);
-                    S2[i] = fmaf(An, gv, S2[i]);
-                    dAp = fmaf(dtf[i], gv, dAp);
-                    Cv[i] = dh;
-                }
+                    for (int m = 0; m < 4; ++m) {
 #pragma unroll
-                for (int off = 16; off > 0; off >>= 1) dAp += __shfl_xor_sync(FULL, dAp, off);
+                        for (int s = 0; s < 2; ++s) {
+                            const float2 bb = unpack2(b2[s][m]);
+                            const float h0 = fmaf(a[s][2 * m], hp[s], bb.x);
+                            const float h1 = fmaf(a[s][2 * m + 1], h0, bb.y);
+                            h2[s][m] = pack2(h0, h1);
+                            hp[s] = h1;
+                        }
+                    }
+#pragma unroll
+                    for (int m = 3; m >= 0; --m) {
+#pragma unroll
+                        for (int s = 0; s < 2; ++s) {
+                            const float d1 = e[s][2 * m + 1] + carry[s];
+                            carry[s] = a[s][2 * m + 1] * d1;
+                            const float d0 = e[s][2 * m] + carry[s];
+                            carry[s] = a[s][2 * m] * d0;
+                            dh2[s][m] = pack2(d0, d1);
+                        }
+                    }
+                }
                 if (lane == 0) {
-                    S.DHC[cg][w][n] = carry;  // carry into the previous chunk
-                    S.DAACC[cg][w][n] += dAp;
+                    S.DHC[cg][w][n0] = carry[0];  // carries into the previous chunk
+                    if (has1) S.DHC[cg][w][n0 + 1] = carry[1];
                 }
-                // dB / dC partials of this warp's channel -> reduce over the CTA's warps
-                {
-                    float dBv[8], dCv[8];
+                // per-step gradients, as pairs; dB / dC partials go to the CTA reduction
+                f32x2 dA2[2] = {pack2(0.f, 0.f), pack2(0.f, 0.f)};
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        dBv[i] = Cv[i] * dtu[i];
-                        dCv[i] = dog[i] * h[i];
+                for (int s = 0; s < 2; ++s) {
+                    float *rb = &S.RED[s][w][0][0];
+#pragma unroll
+                    for (int m = 0; m < 4; ++m) {
+                        const f32x2 pv = fma2(dtu2[m] ^ 0x8000000080000000ull, Bv[s][m], h2[s][m]);  // a_t h_{t-1}
+                        const f32x2 gv = mul2(dh2[s][m], pv);
+                        S1[m] = fma2(dh2[s][m], Bv[s][m], S1[m]);
+                        S2[m] = fma2(Anp[s], gv, S2[m]);
+                        dA2[s] = fma2(dtf2[m], gv, dA2[s]);
+                        const int pos = (m >> 1) * 128 + lane * 4 + (m & 1) * 2;
+                        *reinterpret_cast<f32x2 *>(rb + pos) = mul2(dh2[s][m], dtu2[m]);
+                        *reinterpret_cast<f32x2 *>(rb + CK + pos) = mul2(dog2[m], h2[s][m]);
                     }
-                    st8(&S.RED[n & 1][w][0][0], lane, dBv);
-                    st8(&S.RED[n & 1][w][1][0], lane, dCv);
                 }
                 __syncthreads();
                 {
                     const int q = tid >> 7, pp = (tid & 127) * 2;
-                    float2 s = make_float2(0.f, 0.f);
 #pragma unroll
-                    for (int ww = 0; ww < W; ++ww) {
-                        const float2 v = *reinterpret_cast<const float2 *>(&S.RED[n & 1][ww][q][pp]);
-                        s.x += v.x;
-                        s.y += v.y;
+                    for (int s = 0; s < 2; ++s) {
+                        if (s == 1 && !has1) break;
+                        f32x2 sum = pack2(0.f, 0.f);
+#pragma unroll
+                        for (int ww = 0; ww < W; ++ww)
+                            sum = add2(sum, *reinterpret_cast<const f32x2 *>(&S.RED[s][ww][q][pp]));
+                        f32x2 *acc = reinterpret_cast<f32x2 *>(&S.ACC[q][n0 + s][pp]);
+                        *acc = add2(*acc, sum);
                     }
-                    float2 *acc = reinterpret_cast<float2 *>(&S.ACC[q][n][pp]);
-                    float2 cur = *acc;
-                    cur.x += s.x;
-                    cur.y += s.y;
-                    *acc = cur;
                 }
+#pragma unroll
+                for (int s = 0; s < 2; ++s) {  // this channel's dA: sum over the lanes
+                    const float2 v = unpack2(dA2[s]);
+                    float dAp = v.x + v.y;
+#pragma unroll
+                    for (int off = 16; off > 0; off >>= 1) dAp += __shfl_xor_sync(FULL, dAp, off);
+                    if (lane == 0 && (s == 0 || has1)) S.DAACC[cg][w][n0 + s] += dAp;
+                }
+                __syncthreads();  // RED is rewritten by the next pair
             }
             // ---- per-element epilogue
             {
                 const float Dv = p.D ? p.D[(int64_t)d * p.D_s] : 0.f;
-                float du[8], dd[8], dv[8], dDp = 0.f, dbp = 0.f;
-                load_items(reinterpret_cast<const T *>(p.delta) + (int64_t)b * p.delta_bs + (int64_t)d * p.delta_ds,
-                           t0, L, vec, dv);
-                const float bias = p.delta_bias ? p.delta_bias[(int64_t)d * p.delta_bias_s] : 0.f;
+                float du[8], dd[8], dDp = 0.f, dbp = 0.f;
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const float x = dv[i] + bias;
-                    const float gate = (p.softplus && x <= 20.f) ? sigmoidf_(x) : 1.f;
-                    du[i] = fmaf(dtf[i], S1[i], Dv * dog[i]);
-                    dd[i] = fmaf(uf[i], S1[i], S2[i]) * gate;
-                    if (t0 + i < L) {
-                        dDp = fmaf(dog[i], uf[i], dDp);
-                        dbp += dd[i];
+                for (int m = 0; m < 4; ++m) {
+                    const float2 s1 = unpack2(S1[m]), s2 = unpack2(S2[m]), df = unpack2(dtf2[m]);
+                    const float2 dg = unpack2(dog2[m]), u = unpack2(uf2[m]);
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int i = 2 * m + h;
+                        const float S1v = h ? s1.y : s1.x, S2v = h ? s2.y : s2.x, dtv = h ? df.y : df.x;
+                        const float dgv = h ? dg.y : dg.x, uv = h ? u.y : u.x;
+                        // softplus'(x) = sigmoid(x) = 1 - exp(-softplus(x)); 1 above the threshold
+                        const float gate = p.softplus ? (dtv > 20.f ? 1.f : 1.f - ex2(-dtv * kLog2e)) : 1.f;
+                        du[i] = fmaf(dtv, S1v, Dv * dgv);
+                        dd[i] = fmaf(uv, S1v, S2v) * gate;
+                        if (t0 + i < L) {
+                            dDp = fmaf(dgv, uv, dDp);
+                            dbp += dd[i];
+                        }
                     }
                 }
                 if (valid) {
@@ -386,7 +546,7 @@ cudaError_t launch_acc_to_out(const float *acc, int64_t lpitch, void *out, int i
 template <typename T, bool HAS_Z>
 static cudaError_t launch_bwd_t(const BwdParams &p, cudaStream_t st) {
     auto kern = ss_bwd_kernel<T, HAS_Z>;
-    constexpr int SMEM = (int)sizeof(BwdSmem);
+    constexpr int SMEM = (int)sizeof(BwdSmemT<T>);
     static bool configured = false;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
