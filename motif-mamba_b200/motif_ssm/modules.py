@@ -1,0 +1,277 @@
+"""MotifMamba mixer and LM stack on this library's kernels (callers of the hot path).
+
+* ``Mambamotif`` -- the reference mixer (``mamba_ssm/modules/mamba_simplemotif.py:31-443``)
+  for ``pq_rank = 0`` (the motif P/Q path is not built and raises).  Parameter names,
+  shapes and initialisation follow the reference (dt-bias inverse-softplus init ``:102-110``,
+  S4D-real ``A_log`` ``:116-123``, ``D = 1`` ``:135``).  Prefill runs ``mamba_inner_fn``
+  (fused conv -> x_proj -> dt_proj -> scan -> out_proj); with an inference cache it runs
+  conv + ``selective_scan_fn`` and stores the decode states; ``step`` runs
+  ``causal_conv1d_update`` + ``selective_state_update``.
+* ``Block``, ``MixerModel``, ``MambaLMHeadModel`` -- the pre-norm residual stack of
+  ``mamba_ssm/models/mixer_seq_simple.py:118-309`` (the export lacks ``Block`` and
+  ``RMSNorm``; their semantics -- Add -> Norm -> Mixer, residual kept in fp32 when
+  ``residual_in_fp32`` -- are restated from ``:142-146, 190-211``).  RMSNorm is
+  ``x * rsqrt(mean(x^2) + eps) * w``.
+"""
+import math
+from dataclasses import dataclass, field
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .causal_conv1d import causal_conv1d_fn, causal_conv1d_update
+from .selective_scan_interface import mamba_inner_fn, selective_scan_fn
+from .selective_state_update import selective_state_update
+
+
+class Mambamotif(nn.Module):
+    SIZE_PRESETS = {
+        "tiny": {"d_model": 256, "d_state": 16, "d_conv": 4, "expand": 2},
+        "small": {"d_model": 512, "d_state": 32, "d_conv": 4, "expand": 2},
+        "base": {"d_model": 768, "d_state": 64, "d_conv": 4, "expand": 2},
+    }
+
+    def __init__(self, d_model, d_state=16, d_conv=4, expand=2, dt_rank="auto", dt_min=0.001, dt_max=0.1,
+                 dt_init="random", dt_scale=1.0, dt_init_floor=1e-4, conv_bias=True, bias=False,
+                 use_fast_path=True, layer_idx=None, pq_rank=0, pq_per_dim=False, pq_k_init=1e-4,
+                 device=None, dtype=None):
+        if pq_rank:
+            raise NotImplementedError("Mambamotif: the P/Q (motif low-rank) path is not built in this library")
+        fk = {"device": device, "dtype": dtype}
+        super().__init__()
+        self.d_model, self.d_state, self.d_conv, self.expand = d_model, d_state, d_conv, expand
+        self.d_inner = int(expand * d_model)
+        self.dt_rank = math.ceil(d_model / 16) if dt_rank == "auto" else dt_rank
+        self.use_fast_path = use_fast_path
+        self.layer_idx = layer_idx
+        self.in_proj = nn.Linear(d_model, self.d_inner * 2, bias=bias, **fk)
+        self.conv1d = nn.Conv1d(self.d_inner, self.d_inner, kernel_size=d_conv, groups=self.d_inner,
+                                padding=d_conv - 1, bias=conv_bias, **fk)
+        self.activation = "silu"
+        self.x_proj = nn.Linear(self.d_inner, self.dt_rank + d_state * 2, bias=False, **fk)
+        self.dt_proj = nn.Linear(self.dt_rank, self.d_inner, bias=True, **fk)
+        std = self.dt_rank ** -0.5 * dt_scale
+        if dt_init == "constant":
+            nn.init.constant_(self.dt_proj.weight, std)
+        elif dt_init == "random":
+            nn.init.uniform_(self.dt_proj.weight, -std, std)
+        else:
+            raise NotImplementedError(dt_init)
+        dt = torch.exp(torch.rand(self.d_inner, **fk) * (math.log(dt_max) - math.log(dt_min))
+                       + math.log(dt_min)).clamp(min=dt_init_floor)
+        with torch.no_grad():
+            self.dt_proj.bias.copy_(dt + torch.log(-torch.expm1(-dt)))  # inverse softplus
+        self.dt_proj.bias._no_reinit = True
+        A = torch.arange(1, d_state + 1, dtype=torch.float32, device=device).repeat(self.d_inner, 1)
+        self.A_log = nn.Parameter(torch.log(A))
+        self.A_log._no_weight_decay = True
+        self.D = nn.Parameter(torch.ones(self.d_inner, device=device))
+        self.D._no_weight_decay = True
+        self.register_parameter("P", None)
+        self.register_parameter("Q", None)
+        self.register_parameter("pq_k", None)
+        self.out_proj = nn.Linear(self.d_inner, d_model, bias=bias, **fk)
+
+    def forward(self, hidden_states, inference_params=None):
+        """hidden_states (B, L, D) -> (B, L, D)."""
+        batch, seqlen, _ = hidden_states.shape
+        conv_state = ssm_state = None
+        if inference_params is not None:
+            conv_state, ssm_state = self._get_states_from_cache(inference_params, batch)
+            if inference_params.seqlen_offset > 0:
+                out, _, _ = self.step(hidden_states, conv_state, ssm_state)
+                return out
+        # in_proj and the (b l d) -> (b d l) transpose in one GEMM (mamba_simplemotif.py:257-261)
+        xz = (self.in_proj.weight @ hidden_states.reshape(-1, self.d_model).t()).view(-1, batch, seqlen)
+        xz = xz.transpose(0, 1)
+        if self.in_proj.bias is not None:
+            xz = xz + self.in_proj.bias.to(xz.dtype).unsqueeze(-1)
+        A = -torch.exp(self.A_log.float())
+        if self.use_fast_path and inference_params is None:
+            return mamba_inner_fn(xz, self.conv1d.weight, self.conv1d.bias, self.x_proj.weight,
+                                  self.dt_proj.weight, self.out_proj.weight, self.out_proj.bias, A, None, None,
+                                  self.D.float(), delta_bias=self.dt_proj.bias.float(), delta_softplus=True)
+        x, z = xz.chunk(2, dim=1)
+        if conv_state is not None:
+            conv_state.copy_(F.pad(x, (self.d_conv - x.shape[-1], 0)))
+        x = causal_conv1d_fn(x, self.conv1d.weight.reshape(self.d_inner, -1), self.conv1d.bias,
+                             activation=self.activation)
+        x_dbl = self.x_proj(x.transpose(1, 2).reshape(-1, self.d_inner))
+        dt, B, C = torch.split(x_dbl, [self.dt_rank, self.d_state, self.d_state], dim=-1)
+        dt = (self.dt_proj.weight @ dt.t()).view(self.d_inner, batch, seqlen).transpose(0, 1)
+        B = B.view(batch, seqlen, -1).transpose(1, 2).contiguous()
+        C = C.view(batch, seqlen, -1).transpose(1, 2).contiguous()
+        y = selective_scan_fn(x, dt, A, B, C, self.D.float(), z=z, delta_bias=self.dt_proj.bias.float(),
+                              delta_softplus=True, return_last_state=ssm_state is not None)
+        if ssm_state is not None:
+            y, last_state = y
+            ssm_state.copy_(last_state)
+        return self.out_proj(y.transpose(1, 2))
+
+    def step(self, hidden_states, conv_state, ssm_state):
+        """One decode token (mamba_simplemotif.py:337-402); states are updated in place."""
+        assert hidden_states.shape[1] == 1, "decoding one token at a time"
+        xz = self.in_proj(hidden_states.squeeze(1))
+        x, z = xz.chunk(2, dim=-1)
+        x = causal_conv1d_update(x, conv_state, self.conv1d.weight.reshape(self.d_inner, -1), self.conv1d.bias,
+                                 self.activation)
+        x_db = self.x_proj(x)
+        dt, B, C = torch.split(x_db, [self.dt_rank, self.d_state, self.d_state], dim=-1)
+        dt = F.linear(dt, self.dt_proj.weight)
+        A = -torch.exp(self.A_log.float())
+        y = selective_state_update(ssm_state, x, dt, A, B, C, self.D, z=z, dt_bias=self.dt_proj.bias,
+                                   dt_softplus=True)
+        return self.out_proj(y).unsqueeze(1), conv_state, ssm_state
+
+    def allocate_inference_cache(self, batch_size, max_seqlen, dtype=None, **kwargs):
+        device = self.out_proj.weight.device
+        conv_state = torch.zeros(batch_size, self.d_inner, self.d_conv, device=device,
+                                 dtype=self.conv1d.weight.dtype if dtype is None else dtype)
+        ssm_state = torch.zeros(batch_size, self.d_inner, self.d_state, device=device,
+                                dtype=self.dt_proj.weight.dtype if dtype is None else dtype)
+        return conv_state, ssm_state
+
+    def _get_states_from_cache(self, inference_params, batch_size):
+        assert self.layer_idx is not None
+        cache = inference_params.key_value_memory_dict
+        if self.layer_idx not in cache:
+            cache[self.layer_idx] = self.allocate_inference_cache(batch_size, inference_params.max_seqlen)
+        return cache[self.layer_idx]
+
+
+@dataclass
+class InferenceParams:
+    """Decode cache: per-layer (conv_state, ssm_state) and the number of tokens seen."""
+    max_seqlen: int
+    max_batch_size: int
+    seqlen_offset: int = 0
+    key_value_memory_dict: dict = field(default_factory=dict)
+
+
+class RMSNorm(nn.Module):
+    def __init__(self, hidden_size, eps=1e-5, device=None, dtype=None):
+        super().__init__()
+        self.eps = eps
+        self.weight = nn.Parameter(torch.ones(hidden_size, device=device, dtype=dtype))
+
+    def forward(self, x):
+        return F.rms_norm(x, (x.shape[-1],), self.weight, self.eps)
+
+
+class Block(nn.Module):
+    """Add -> Norm -> Mixer (mixer_seq_simple.py:142-146): returns (mixer_out, residual)."""
+
+    def __init__(self, dim, mixer, norm, residual_in_fp32=True):
+        super().__init__()
+        self.mixer, self.norm, self.residual_in_fp32 = mixer, norm, residual_in_fp32
+
+    def forward(self, hidden_states, residual=None, inference_params=None):
+        residual = hidden_states if residual is None else hidden_states + residual
+        hidden_states = self.norm(residual.to(self.norm.weight.dtype))
+        if self.residual_in_fp32:
+            residual = residual.float()
+        return self.mixer(hidden_states, inference_params=inference_params), residual
+
+    def allocate_inference_cache(self, batch_size, max_seqlen, dtype=None, **kw):
+        return self.mixer.allocate_inference_cache(batch_size, max_seqlen, dtype=dtype, **kw)
+
+
+@dataclass
+class MambaConfig:
+    """Same fields and defaults as the reference (mamba_ssm/models/config_mamba.py:4-18)."""
+    d_model: int = 2560
+    d_intermediate: int = 0
+    n_layer: int = 64
+    vocab_size: int = 50277
+    ssm_cfg: dict = field(default_factory=dict)
+    attn_layer_idx: list = field(default_factory=list)
+    attn_cfg: dict = field(default_factory=dict)
+    rms_norm: bool = True
+    residual_in_fp32: bool = True
+    fused_add_norm: bool = True
+    pad_vocab_size_multiple: int = 8
+    tie_embeddings: bool = True
+
+
+def _init_weights(module, n_layer, initializer_range=0.02, rescale_prenorm_residual=True, n_residuals_per_layer=1):
+    """GPT-2 style init of the reference stack (mixer_seq_simple.py:86-115)."""
+    if isinstance(module, nn.Linear):
+        if module.bias is not None and not getattr(module.bias, "_no_reinit", False):
+            nn.init.zeros_(module.bias)
+    elif isinstance(module, nn.Embedding):
+        nn.init.normal_(module.weight, std=initializer_range)
+    if rescale_prenorm_residual:
+        for name, p in module.named_parameters():
+            if name in ("out_proj.weight", "fc2.weight"):
+                nn.init.kaiming_uniform_(p, a=math.sqrt(5))
+                with torch.no_grad():
+                    p /= math.sqrt(n_residuals_per_layer * n_layer)
+
+
+class MixerModel(nn.Module):
+    def __init__(self, d_model, n_layer, vocab_size, ssm_cfg=None, norm_epsilon=1e-5, rms_norm=True,
+                 residual_in_fp32=True, device=None, dtype=None, **unused):
+        fk = {"device": device, "dtype": dtype}
+        super().__init__()
+        ssm_cfg = dict(ssm_cfg or {})
+        ssm_cfg.pop("layer", None)
+        self.embedding = nn.Embedding(vocab_size, d_model, **fk)
+        norm_cls = (lambda: RMSNorm(d_model, eps=norm_epsilon, **fk)) if rms_norm else \
+            (lambda: nn.LayerNorm(d_model, eps=norm_epsilon, **fk))
+        self.layers = nn.ModuleList([
+            Block(d_model, Mambamotif(d_model, layer_idx=i, **ssm_cfg, **fk), norm_cls(), residual_in_fp32)
+            for i in range(n_layer)])
+        self.norm_f = norm_cls()
+        self.apply(lambda m: _init_weights(m, n_layer))
+
+    def allocate_inference_cache(self, batch_size, max_seqlen, dtype=None, **kw):
+        return {i: l.allocate_inference_cache(batch_size, max_seqlen, dtype=dtype, **kw)
+                for i, l in enumerate(self.layers)}
+
+    def forward(self, input_ids, inference_params=None):
+        hidden, residual = self.embedding(input_ids), None
+        for layer in self.layers:
+            hidden, residual = layer(hidden, residual, inference_params=inference_params)
+        residual = hidden + residual if residual is not None else hidden
+        return self.norm_f(residual.to(self.norm_f.weight.dtype))
+
+
+class MambaLMHeadModel(nn.Module):
+    """Embedding -> MixerModel -> tied lm_head (mixer_seq_simple.py:215-309)."""
+
+    def __init__(self, config: MambaConfig, device=None, dtype=None):
+        super().__init__()
+        self.config = config
+        vocab = config.vocab_size
+        if vocab % config.pad_vocab_size_multiple:
+            vocab += config.pad_vocab_size_multiple - vocab % config.pad_vocab_size_multiple
+        self.backbone = MixerModel(config.d_model, config.n_layer, vocab, ssm_cfg=config.ssm_cfg,
+                                   rms_norm=config.rms_norm, residual_in_fp32=config.residual_in_fp32,
+                                   device=device, dtype=dtype)
+        self.lm_head = nn.Linear(config.d_model, vocab, bias=False, device=device, dtype=dtype)
+        if config.tie_embeddings:
+            self.lm_head.weight = self.backbone.embedding.weight
+
+    def allocate_inference_cache(self, batch_size, max_seqlen, dtype=None, **kw):
+        return self.backbone.allocate_inference_cache(batch_size, max_seqlen, dtype=dtype, **kw)
+
+    def forward(self, input_ids, inference_params=None, num_last_tokens=0):
+        hidden = self.backbone(input_ids, inference_params=inference_params)
+        if num_last_tokens > 0:
+            hidden = hidden[:, -num_last_tokens:]
+        return self.lm_head(hidden)
+
+    @torch.no_grad()
+    def generate_greedy(self, input_ids, max_new_tokens):
+        """Prefill with the inference cache, then greedy decode one token per step."""
+        batch = input_ids.shape[0]
+        params = InferenceParams(max_seqlen=input_ids.shape[1] + max_new_tokens, max_batch_size=batch)
+        logits = self.forward(input_ids, inference_params=params, num_last_tokens=1)
+        params.seqlen_offset = input_ids.shape[1]
+        out = [logits.argmax(-1)]
+        for _ in range(max_new_tokens - 1):
+            logits = self.forward(out[-1], inference_params=params, num_last_tokens=1)
+            params.seqlen_offset += 1
+            out.append(logits.argmax(-1))
+        return torch.cat(out, dim=1)
