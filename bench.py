@@ -226,12 +226,17 @@ def main():
     ap.add_argument("--batch", type=int, default=None,
                     help="override the per-GPU batch (profiling a smaller case of the same kernels)")
     ap.add_argument("--seqlen", type=int, default=None, help="override the sequence length")
+    ap.add_argument("--workload", default="scan", choices=["scan", "prefill"],
+                    help="scan: selective scan fwd+bwd, config 4 (default); prefill: 24-layer config-2 stack, "
+                         "prefill tok/s (global batch 16 x 4096, strong scaling) plus greedy decode tok/s")
     args = ap.parse_args()
     if args.batch:
         CFG["batch"] = args.batch
     if args.seqlen:
         CFG["seqlen"] = args.seqlen
     args.warmup = max(args.warmup, 3)
+    if args.workload == "prefill":
+        return run_prefill(args)
     if args.impl == "reference":
         return run_reference(args)
 
@@ -383,6 +388,149 @@ def run_e2e(t, dout, dev, stream, world, selective_scan_fn, algo, steps, dist):
     return {"value": algo * world / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms, "steps": steps,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "api": "motif_ssm.selective_scan_fn forward + autograd backward, pinned host buffers"}
+
+
+PREFILL = dict(n_layer=24, d_model=768, vocab=512, d_state=16, global_batch=16, seqlen=4096,
+               decode_batch=64, decode_steps=256, prompt=128)
+
+
+def _cpu_prefill_tok_s(threads, seqlen=512):
+    """The reference's CPU path for one layer of the stack (oracle restatement of the
+    mixer: conv, x_proj, dt_proj, selective_scan_ref, out_proj, fp32), extrapolated
+    to 24 layers: tok/s = tokens / (24 * seconds per layer)."""
+    from oracle import ssm_oracle as O
+    torch.set_num_threads(threads)
+    d, di, n, r = PREFILL["d_model"], 2 * PREFILL["d_model"], PREFILL["d_state"], 48
+    g = torch.Generator().manual_seed(0)
+    xz = torch.randn(1, 2 * di, seqlen, generator=g)
+    w = [0.02 * torch.randn(di, 1, 4, generator=g), 0.02 * torch.randn(di, generator=g),
+         0.02 * torch.randn(r + 2 * n, di, generator=g), 0.1 * torch.randn(di, r, generator=g),
+         0.02 * torch.randn(d, di, generator=g)]
+    A = -torch.arange(1, n + 1, dtype=torch.float32).repeat(di, 1)
+    t0 = time.perf_counter()
+    with torch.no_grad():
+        O.mamba_inner_ref(xz, *w, None, A, None, None, torch.ones(di), delta_bias=torch.full((di,), -4.0))
+    dt = time.perf_counter() - t0
+    return dict(value=seqlen / (dt * PREFILL["n_layer"]), unit="tok/s", cores=threads, kind="port",
+                sample=f"one mixer layer (d_model 768, d_inner 1536) at batch 1 x {seqlen} tokens through the "
+                       f"oracle restatement of mamba_inner_ref in fp32: {dt:.2f} s, extrapolated to 24 layers")
+
+
+def run_prefill(args):
+    """Config 2: 24-layer MotifMamba stack, bf16 random init, vocab 512 random ids.
+    Prefill of a fixed global batch of 16 x 4096 split over ranks (strong scaling; no
+    collective: each rank runs its own rows), then 256 greedy decode steps at global
+    batch 64 through the cache (conv / state update kernels)."""
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if rank == 0:
+            cb = _cpu_prefill_tok_s(os.cpu_count() or 1)
+            print(json.dumps({"impl": "reference", "metric": "MotifMamba prefill tok/s (config 2)", "value": cb["value"],
+                              "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                              "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
+                              "data": "synthetic", "config": {"workload": "24-layer config-2 prefill"},
+                              "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": "tok/s",
+                                                          "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+        return 0
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    from motif_ssm.modules import InferenceParams, MambaConfig, MambaLMHeadModel
+    P = PREFILL
+    torch.manual_seed(0)
+    model = MambaLMHeadModel(MambaConfig(d_model=P["d_model"], n_layer=P["n_layer"], vocab_size=P["vocab"],
+                                         ssm_cfg={"d_state": P["d_state"]}), device=dev, dtype=torch.bfloat16)
+    model.eval()
+    bl = max(1, P["global_batch"] // world)
+    g = torch.Generator(device=dev).manual_seed(rank)
+    ids = torch.randint(0, P["vocab"], (bl, P["seqlen"]), device=dev, generator=g)
+    stream = torch.cuda.current_stream(dev)
+
+    def prefill():
+        with torch.no_grad():
+            return model(ids, num_last_tokens=1)
+
+    for _ in range(args.warmup):
+        prefill()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        s.record(stream)
+        for _ in range(args.steps):
+            prefill()
+        e.record(stream)
+        torch.cuda.synchronize()
+    tt = torch.tensor([s.elapsed_time(e) / args.steps], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    ms = tt.item()
+    value = bl * world * P["seqlen"] / (ms * 1e-3)
+
+    # greedy decode through the cache
+    db = max(1, P["decode_batch"] // world)
+    prompt = torch.randint(0, P["vocab"], (db, P["prompt"]), device=dev, generator=g)
+    with torch.no_grad():
+        params = InferenceParams(max_seqlen=P["prompt"] + P["decode_steps"], max_batch_size=db)
+        tok = model(prompt, inference_params=params, num_last_tokens=1).argmax(-1)
+        params.seqlen_offset = P["prompt"]
+        for _ in range(3):  # warm-up steps on a copy of the cache
+            model(tok, inference_params=InferenceParams(max_seqlen=8, max_batch_size=db,
+                                                         seqlen_offset=1,
+                                                         key_value_memory_dict={k: (a.clone(), b.clone()) for k, (a, b) in params.key_value_memory_dict.items()}),
+                  num_last_tokens=1)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        s.record(stream)
+        for _ in range(P["decode_steps"]):
+            tok = model(tok, inference_params=params, num_last_tokens=1).argmax(-1)
+            params.seqlen_offset += 1
+        e.record(stream)
+        torch.cuda.synchronize()
+    td = torch.tensor([s.elapsed_time(e)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(td, op=dist.ReduceOp.MAX)
+    decode_tok_s = db * world * P["decode_steps"] / (td.item() * 1e-3)
+
+    # end to end: host ids in, last-token logits out
+    host_ids = ids.cpu().pin_memory()
+    dev_ids = torch.empty_like(ids)
+    out_host = torch.empty((bl, 1, model.lm_head.weight.shape[0]), dtype=torch.bfloat16).pin_memory()
+    s.record(stream)
+    for _ in range(args.steps):
+        dev_ids.copy_(host_ids, non_blocking=True)
+        with torch.no_grad():
+            lg = model(dev_ids, num_last_tokens=1)
+        out_host.copy_(lg, non_blocking=True)
+    e.record(stream)
+    torch.cuda.synchronize()
+    te = torch.tensor([s.elapsed_time(e) / args.steps], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    cpu = _cpu_prefill_tok_s(os.cpu_count() or 1) if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
+    if rank == 0:
+        print(json.dumps({
+            "metric": "MotifMamba prefill tok/s (config 2)", "value": value, "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "24-layer MotifMamba stack (d_model 768, d_inner 1536, n 16, RMSNorm, vocab 512), "
+                                   "bf16 random init, prefill of global batch 16 x 4096 random ids, last-token logits",
+                       "global_batch": bl * world, "seqlen": P["seqlen"], "parallelism": f"batch-sharded x{world}"},
+            "decode_tok_s": decode_tok_s, "decode": {"global_batch": db * world, "steps": P["decode_steps"],
+                                                     "prompt": P["prompt"]},
+            "gpu_launches": None, "clocks": clk.summary(),
+            "e2e": {"value": bl * world * P["seqlen"] / (te.item() * 1e-3), "unit": "tok/s",
+                    "h2d_bytes_per_step": host_ids.numel() * 8, "d2h_bytes_per_step": out_host.numel() * 2},
+            "cpu_baseline": cpu}), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
 
 
 if __name__ == "__main__":
