@@ -226,9 +226,10 @@ def main():
     ap.add_argument("--batch", type=int, default=None,
                     help="override the per-GPU batch (profiling a smaller case of the same kernels)")
     ap.add_argument("--seqlen", type=int, default=None, help="override the sequence length")
-    ap.add_argument("--workload", default="scan", choices=["scan", "prefill"],
+    ap.add_argument("--workload", default="scan", choices=["scan", "prefill", "tp"],
                     help="scan: selective scan fwd+bwd, config 4 (default); prefill: 24-layer config-2 stack, "
-                         "prefill tok/s (global batch 16 x 4096, strong scaling) plus greedy decode tok/s")
+                         "prefill tok/s (global batch 16 x 4096, strong scaling) plus greedy decode tok/s; "
+                         "tp: 64-layer config-3 stack, prefill 1 x 32768 with d_inner sharded over the GPUs")
     args = ap.parse_args()
     if args.batch:
         CFG["batch"] = args.batch
@@ -237,6 +238,8 @@ def main():
     args.warmup = max(args.warmup, 3)
     if args.workload == "prefill":
         return run_prefill(args)
+    if args.workload == "tp":
+        return run_tp(args)
     if args.impl == "reference":
         return run_reference(args)
 
@@ -528,6 +531,67 @@ def run_prefill(args):
             "e2e": {"value": bl * world * P["seqlen"] / (te.item() * 1e-3), "unit": "tok/s",
                     "h2d_bytes_per_step": host_ids.numel() * 8, "d2h_bytes_per_step": out_host.numel() * 2},
             "cpu_baseline": cpu}), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def run_tp(args):
+    """Config 3: 64-layer stack (d_model 2560, d_inner 5120, n 16, dt_rank 160), bf16 random
+    init, prefill of 1 x 32768 tokens with d_inner channel-sharded over the ranks and two
+    NCCL all-reduces per layer (x_dbl partial sums, out_proj partial sums)."""
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "the tp workload has no CPU reference run; "
+                              "use the default scan workload for the reference arm"}))
+        return 0
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    group = None
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    from motif_ssm.modules import MambaConfig, MambaLMHeadModel, shard_model_tp
+    L = args.seqlen or 32768
+    n_layer = 64
+    torch.manual_seed(0)
+    model = MambaLMHeadModel(MambaConfig(d_model=2560, n_layer=n_layer, vocab_size=50277,
+                                         ssm_cfg={"d_state": 16}), device=dev, dtype=torch.bfloat16)
+    shard_model_tp(model, rank, world, group)
+    torch.cuda.empty_cache()
+    ids = torch.randint(0, 50277, (1, L), device=dev, generator=torch.Generator(device=dev).manual_seed(0))
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        with torch.no_grad():
+            return model(ids, num_last_tokens=1)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        s.record(stream)
+        for _ in range(args.steps):
+            step()
+        e.record(stream)
+        torch.cuda.synchronize()
+    tt = torch.tensor([s.elapsed_time(e) / args.steps], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    if rank == 0:
+        print(json.dumps({
+            "metric": "MotifMamba TP prefill tok/s (config 3)", "value": L / (tt.item() * 1e-3), "unit": "tok/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": tt.item(),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "64-layer stack d_model 2560 d_inner 5120 n 16 dt_rank 160, bf16 random init, "
+                                   "prefill 1 x %d, last-token logits" % L, "parallelism": f"tp{world}"},
+            "clocks": clk.summary(), "e2e": None, "cpu_baseline": None}), flush=True)
     if world > 1:
         dist.destroy_process_group()
     return 0

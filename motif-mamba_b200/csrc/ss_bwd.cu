@@ -261,10 +261,11 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
             for (int m = 0; m < 4; ++m) S1[m] = S2[m] = pack2(0.f, 0.f);
             // A row and the chunk-start states of this channel, read once per pass (off the
             // per-state dependency chain)
-            if (lane < p.dstate) {
-                S.AX[w][0][lane] = valid ? p.A[(int64_t)d * p.A_ds + (int64_t)lane * p.A_ns] : 0.f;
+            if (lane < NS) {  // states >= dstate read as zero (A, state), like their zero B / C rows
+                const bool st = valid && lane < p.dstate;
+                S.AX[w][0][lane] = st ? p.A[(int64_t)d * p.A_ds + (int64_t)lane * p.A_ns] : 0.f;
                 S.AX[w][1][lane] =
-                    (k > 0 && valid) ? p.x[(row * p.n_chunks + (k - 1)) * 2 * p.dstate + 2 * lane + 1] : 0.f;
+                    (k > 0 && st) ? p.x[(row * p.n_chunks + (k - 1)) * 2 * p.dstate + 2 * lane + 1] : 0.f;
             }
             __syncwarp();
 
@@ -281,15 +282,14 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
 #pragma unroll
                 for (int s = 0; s < 2; ++s) {
                     const int n = n0 + s;
-                    An[s] = (s == 0 || has1) ? S.AX[w][0][n] : 0.f;
+                    An[s] = S.AX[w][0][n];  // n < NS always (dstate <= 16); padded states are zero
                     A2[s] = An[s] * kLog2e;
                     A2p[s] = pack2(A2[s], A2[s]);
                     Anp[s] = pack2(An[s], An[s]);
                     float bv8[8];
-                    bc_ld8(&S.BC[0][s == 0 || has1 ? n : n0][0], lane, bv8);
-                    const float z = (s == 0 || has1) ? 1.f : 0.f;
+                    bc_ld8(&S.BC[0][n][0], lane, bv8);
 #pragma unroll
-                    for (int m = 0; m < 4; ++m) Bv[s][m] = pack2(z * bv8[2 * m], z * bv8[2 * m + 1]);
+                    for (int m = 0; m < 4; ++m) Bv[s][m] = pack2(bv8[2 * m], bv8[2 * m + 1]);
 #pragma unroll
                     for (int m = 0; m < 4; ++m) {
                         const float2 v = unpack2(ex2x2(mul2(dtf2[m], A2p[s])));
@@ -304,16 +304,15 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
                 float e[2][8];
 #pragma unroll
                 for (int s = 0; s < 2; ++s) {
-                    const int n = (s == 0 || has1) ? n0 + s : n0;
+                    const int n = n0 + s;
                     float cv8[8];
                     bc_ld8(&S.BC[1][n][0], lane, cv8);
                     const float2 e0 = unpack2(mul2(dog2[0], pack2(cv8[0], cv8[1])));
                     const float2 e1 = unpack2(mul2(dog2[1], pack2(cv8[2], cv8[3])));
                     const float2 e2v = unpack2(mul2(dog2[2], pack2(cv8[4], cv8[5])));
                     const float2 e3 = unpack2(mul2(dog2[3], pack2(cv8[6], cv8[7])));
-                    const float z = (s == 0 || has1) ? 1.f : 0.f;
-                    e[s][0] = z * e0.x; e[s][1] = z * e0.y; e[s][2] = z * e1.x; e[s][3] = z * e1.y;
-                    e[s][4] = z * e2v.x; e[s][5] = z * e2v.y; e[s][6] = z * e3.x; e[s][7] = z * e3.y;
+                    e[s][0] = e0.x; e[s][1] = e0.y; e[s][2] = e1.x; e[s][3] = e1.y;
+                    e[s][4] = e2v.x; e[s][5] = e2v.y; e[s][6] = e3.x; e[s][7] = e3.y;
                 }
 #pragma unroll
                 for (int m = 0; m < 4; ++m) {
@@ -363,9 +362,9 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
                 float h_in[2], carry[2];
 #pragma unroll
                 for (int s = 0; s < 2; ++s) {
-                    const int n = (s == 0 || has1) ? n0 + s : n0;
-                    const float h_chunk = (s == 0 || has1) ? S.AX[w][1][n] : 0.f;
-                    const float c_chunk = (s == 0 || has1) ? S.DHC[cg][w][n] : 0.f;
+                    const int n = n0 + s;
+                    const float h_chunk = S.AX[w][1][n];
+                    const float c_chunk = S.DHC[cg][w][n];  // never written for padded states: 0
                     const float Ae = __shfl_up_sync(FULL, Ad[s], 1), He = __shfl_up_sync(FULL, Hd[s], 1);
                     const float Pe = __shfl_down_sync(FULL, Pd[s], 1), Qe = __shfl_down_sync(FULL, Qd[s], 1);
                     h_in[s] = lane == 0 ? h_chunk : fmaf(Ae, h_chunk, He);

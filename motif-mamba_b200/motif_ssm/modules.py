@@ -275,3 +275,82 @@ class MambaLMHeadModel(nn.Module):
             params.seqlen_offset += 1
             out.append(logits.argmax(-1))
         return torch.cat(out, dim=1)
+
+
+# ---------------------------------------------------------------------------------------
+# Channel-sharded tensor parallelism (inference prefill).  d_inner is split over the ranks
+# of `group`: in_proj rows (x and z halves of this rank's channels), conv1d, dt_proj rows,
+# A, D and the scan are local.  x_proj contracts over d_inner, so each rank's x_dbl is a
+# partial sum: all-reduce #1 (b*l x (dt_rank + 2n)) before dt_proj / B / C; out_proj is
+# row-split: all-reduce #2 (b*l x d_model) after it.  Both are NCCL sums on the current
+# stream.  The reference has no TP; this follows the plan of its channel-independent scan.
+# ---------------------------------------------------------------------------------------
+class TPMambamotif(nn.Module):
+    """One mixer's shard.  Build with ``TPMambamotif.from_full(full_mixer, rank, world, group)``."""
+
+    def __init__(self, d_model, d_inner_local, d_state, d_conv, dt_rank, rank, world, group, device=None,
+                 dtype=None):
+        super().__init__()
+        fk = {"device": device, "dtype": dtype}
+        self.d_model, self.d_local, self.d_state, self.d_conv, self.dt_rank = d_model, d_inner_local, d_state, d_conv, dt_rank
+        self.rank, self.world, self.group = rank, world, group
+        self.in_proj_w = nn.Parameter(torch.empty(2 * d_inner_local, d_model, **fk))
+        self.conv_w = nn.Parameter(torch.empty(d_inner_local, d_conv, **fk))
+        self.conv_b = nn.Parameter(torch.empty(d_inner_local, **fk))
+        self.x_proj_w = nn.Parameter(torch.empty(dt_rank + 2 * d_state, d_inner_local, **fk))
+        self.dt_proj_w = nn.Parameter(torch.empty(d_inner_local, dt_rank, **fk))
+        self.dt_proj_b = nn.Parameter(torch.empty(d_inner_local, device=device, dtype=torch.float32))
+        self.A_log = nn.Parameter(torch.empty(d_inner_local, d_state, device=device, dtype=torch.float32))
+        self.D = nn.Parameter(torch.empty(d_inner_local, device=device, dtype=torch.float32))
+        self.out_proj_w = nn.Parameter(torch.empty(d_model, d_inner_local, **fk))
+
+    @classmethod
+    def from_full(cls, full, rank, world, group):
+        di = full.d_inner
+        assert di % world == 0, "d_inner must divide by the tensor-parallel size"
+        dl = di // world
+        lo, hi = rank * dl, (rank + 1) * dl
+        w = full.in_proj.weight
+        m = cls(full.d_model, dl, full.d_state, full.d_conv, full.dt_rank, rank, world, group,
+                device=w.device, dtype=w.dtype)
+        with torch.no_grad():
+            m.in_proj_w.copy_(torch.cat([w[lo:hi], w[di + lo:di + hi]], dim=0))
+            m.conv_w.copy_(full.conv1d.weight[lo:hi, 0])
+            m.conv_b.copy_(full.conv1d.bias[lo:hi])
+            m.x_proj_w.copy_(full.x_proj.weight[:, lo:hi])
+            m.dt_proj_w.copy_(full.dt_proj.weight[lo:hi])
+            m.dt_proj_b.copy_(full.dt_proj.bias[lo:hi].float())
+            m.A_log.copy_(full.A_log[lo:hi])
+            m.D.copy_(full.D[lo:hi])
+            m.out_proj_w.copy_(full.out_proj.weight[:, lo:hi])
+        return m
+
+    def _all_reduce(self, t):
+        if self.world > 1:
+            torch.distributed.all_reduce(t, group=self.group)
+        return t
+
+    @torch.no_grad()
+    def forward(self, hidden_states, inference_params=None):
+        batch, seqlen, _ = hidden_states.shape
+        xz = (self.in_proj_w @ hidden_states.reshape(-1, self.d_model).t()).view(-1, batch, seqlen).transpose(0, 1)
+        x, z = xz.chunk(2, dim=1)
+        x = causal_conv1d_fn(x, self.conv_w, self.conv_b, activation="silu")
+        x_dbl = x.transpose(1, 2).reshape(-1, self.d_local) @ self.x_proj_w.t()
+        x_dbl = self._all_reduce(x_dbl.contiguous())                       # all-reduce #1
+        dt, B, C = torch.split(x_dbl, [self.dt_rank, self.d_state, self.d_state], dim=-1)
+        dt = (self.dt_proj_w @ dt.t()).view(self.d_local, batch, seqlen).transpose(0, 1)
+        B = B.reshape(batch, seqlen, -1).transpose(1, 2).contiguous()
+        C = C.reshape(batch, seqlen, -1).transpose(1, 2).contiguous()
+        y = selective_scan_fn(x, dt, -torch.exp(self.A_log), B, C, self.D, z=z, delta_bias=self.dt_proj_b,
+                              delta_softplus=True)
+        out = y.transpose(1, 2).reshape(-1, self.d_local) @ self.out_proj_w.t()
+        return self._all_reduce(out.contiguous()).view(batch, seqlen, self.d_model)  # all-reduce #2
+
+
+def shard_model_tp(model, rank, world, group=None):
+    """Replace every mixer of a MambaLMHeadModel by its channel shard for `rank` (in place).
+    Embedding, norms and lm_head stay replicated."""
+    for layer in model.backbone.layers:
+        layer.mixer = TPMambamotif.from_full(layer.mixer, rank, world, group)
+    return model
