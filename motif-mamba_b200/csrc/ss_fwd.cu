@@ -23,6 +23,8 @@
 // (a multiple of kChunkLen long): a carry pass computes each segment's end state from
 // zero and its summed dt, then the main pass folds the carries of earlier segments into
 // its initial state (h_in = prod(decay) * h_in + H) and runs the full scan.
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -86,6 +88,16 @@ __global__ void __launch_bounds__(FwdCfg<NS>::CH, FwdCfg<NS>::MINB) ss_fwd_kerne
         h2[m] = pack2(0.f, 0.f);
         A2p[m] = pack2(A2[2 * m], A2[2 * m + 1]);
     }
+    // S4D-real structure A[d, n] = (n + 1) A[d, 0] (the module's init, and every BASELINE
+    // config): then exp(dt A_n) = r^(n+1) with r = exp(dt A_0), one SFU ex2 per step instead
+    // of one per state.  Checked per channel to 1e-6 relative (the -exp(log(n+1)) round trip
+    // of the module's A_log deviates by < 2e-7); a CTA takes the chained path only if all its
+    // channels qualify, otherwise every state gets its own ex2.
+    bool chain_ok = A2[0] != 0.f || !valid;
+#pragma unroll
+    for (int n = 1; n < NS; ++n)
+        if (n < p.dstate) chain_ok = chain_ok && fabsf(A2[n] - (float)(n + 1) * A2[0]) <= 1e-6f * fabsf(A2[n]);
+    const bool chain = __syncthreads_and(chain_ok) != 0;
     float cum = 0.f;  // sum of dt since t = 0 (main pass) or since the segment start (carry pass)
     const int64_t row = (int64_t)b * p.dim + d;
     if (!CARRY && s > 0 && valid) {
@@ -154,21 +166,40 @@ __global__ void __launch_bounds__(FwdCfg<NS>::CH, FwdCfg<NS>::MINB) ss_fwd_kerne
                 cum += v;
             }
             float y[8];
+            auto steps = [&](auto chained) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const f32x2 *bcr = reinterpret_cast<const f32x2 *>(bc + (g8 + j) * BCW);
-                const f32x2 dt2 = pack2(dv[j], dv[j]), du2 = pack2(dtu[j], dtu[j]);
-                f32x2 acc2[2] = {pack2(0.f, 0.f), pack2(0.f, 0.f)};  // two chains of pair sums
+                for (int j = 0; j < 8; ++j) {
+                    const f32x2 *bcr = reinterpret_cast<const f32x2 *>(bc + (g8 + j) * BCW);
+                    const f32x2 du2 = pack2(dtu[j], dtu[j]);
+                    f32x2 acc2[2] = {pack2(0.f, 0.f), pack2(0.f, 0.f)};  // two chains of pair sums
+                    f32x2 ap, q;  // chained path: (r^(2m+1), r^(2m+2)) and the step (r^2, r^2)
+                    if constexpr (decltype(chained)::value) {
+                        const float r = ex2(dv[j] * A2[0]);
+                        const float r2 = r * r;
+                        ap = pack2(r, r2);
+                        q = pack2(r2, r2);
+                    }
+                    const f32x2 dt2 = pack2(dv[j], dv[j]);
 #pragma unroll
-                for (int m = 0; m < NP; ++m) {
-                    const f32x2 a2 = ex2x2(mul2(dt2, A2p[m]));
-                    h2[m] = fma2(a2, h2[m], mul2(du2, bcr[m]));
-                    if constexpr (!CARRY) acc2[m & 1] = fma2(bcr[NP + m], h2[m], acc2[m & 1]);
+                    for (int m = 0; m < NP; ++m) {
+                        f32x2 a2;
+                        if constexpr (decltype(chained)::value) {
+                            if (m > 0) ap = mul2(ap, q);
+                            a2 = ap;
+                        } else {
+                            a2 = ex2x2(mul2(dt2, A2p[m]));
+                        }
+                        h2[m] = fma2(a2, h2[m], mul2(du2, bcr[m]));
+                        if constexpr (!CARRY) acc2[m & 1] = fma2(bcr[NP + m], h2[m], acc2[m & 1]);
+                    }
+                    const float2 accv = unpack2(add2(acc2[0], acc2[1]));
+                    y[j] = accv.x + accv.y;
                 }
-                const float2 accv = unpack2(add2(acc2[0], acc2[1]));
-                const float acc = accv.x + accv.y;
-                y[j] = acc;
-            }
+            };
+            if (chain)
+                steps(std::true_type{});
+            else
+                steps(std::false_type{});
             if constexpr (!CARRY) {
                 float o[8];
 #pragma unroll

@@ -9,7 +9,7 @@ import torch
 
 
 def make_scan_inputs(batch, dim, seqlen, dstate, dtype=torch.float32, groups=0, has_z=True, has_D=True,
-                     has_bias=True, softplus=True, seed=0, device="cpu"):
+                     has_bias=True, softplus=True, seed=0, device="cpu", random_A=False):
     g = torch.Generator().manual_seed(seed)
     u = torch.randn(batch, dim, seqlen, generator=g)
     if softplus:
@@ -17,6 +17,8 @@ def make_scan_inputs(batch, dim, seqlen, dstate, dtype=torch.float32, groups=0, 
     else:
         delta = 0.5 * torch.rand(batch, dim, seqlen, generator=g)
     A = -torch.arange(1, dstate + 1, dtype=torch.float32).repeat(dim, 1).contiguous()
+    if random_A:  # no (n+1) A_0 structure: exercises the per-state exp path
+        A = -torch.exp(0.5 * torch.randn(dim, dstate, generator=g))
     G = groups if groups else 1
     B = torch.randn(batch, G, dstate, seqlen, generator=g)
     C = torch.randn(batch, G, dstate, seqlen, generator=g)

@@ -205,3 +205,21 @@ def test_scan_extreme_delta_and_z():
     ref_out, ref_last, ref_grads = oracle(inp, dout, True)
     out, last, grads = run_kernel(inp, dout, True)
     compare(out, last, grads, ref_out, ref_last, ref_grads, torch.float32, "extreme delta/z")
+
+
+@pytest.mark.parametrize("dtype,seqlen", [(torch.float32, 300), (torch.bfloat16, 700), (torch.float32, 2049)])
+def test_scan_unstructured_A(dtype, seqlen):
+    """A without the S4D-real (n+1) A_0 structure takes the per-state exp path."""
+    inp, dout = make_scan_inputs(2, 40, seqlen, 16, dtype, seed=seqlen + 1, random_A=True)
+    ref_out, ref_last, ref_grads = oracle(inp, dout, True)
+    out, last, grads = run_kernel(inp, dout, True)
+    compare(out, last, grads, ref_out, ref_last, ref_grads, dtype, "random A")
+
+
+def test_scan_mixed_structure_in_one_cta():
+    """Channels with and without the structure side by side in one CTA."""
+    inp, dout = make_scan_inputs(1, 64, 400, 16, torch.float32, seed=77)
+    inp["A"][5] = -torch.exp(torch.randn(16))
+    ref_out, ref_last, ref_grads = oracle(inp, dout, True)
+    out, last, grads = run_kernel(inp, dout, True)
+    compare(out, last, grads, ref_out, ref_last, ref_grads, torch.float32, "mixed A")
