@@ -490,10 +490,11 @@ def run_prefill(args):
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
+        from motif_ssm.modules import GraphedDecoder
+        dec = GraphedDecoder(model, params, db)   # whole decode step as one CUDA graph
         s.record(stream)
         for _ in range(P["decode_steps"]):
-            tok = model(tok, inference_params=params, num_last_tokens=1).argmax(-1)
-            params.seqlen_offset += 1
+            tok = dec.step(tok).argmax(-1)
         e.record(stream)
         torch.cuda.synchronize()
     td = torch.tensor([s.elapsed_time(e)], device=dev, dtype=torch.float64)
@@ -526,7 +527,7 @@ def run_prefill(args):
                                    "bf16 random init, prefill of global batch 16 x 4096 random ids, last-token logits",
                        "global_batch": bl * world, "seqlen": P["seqlen"], "parallelism": f"batch-sharded x{world}"},
             "decode_tok_s": decode_tok_s, "decode": {"global_batch": db * world, "steps": P["decode_steps"],
-                                                     "prompt": P["prompt"]},
+                                                     "prompt": P["prompt"], "cuda_graph": True},
             "gpu_launches": None, "clocks": clk.summary(),
             "e2e": {"value": bl * world * P["seqlen"] / (te.item() * 1e-3), "unit": "tok/s",
                     "h2d_bytes_per_step": host_ids.numel() * 8, "d2h_bytes_per_step": out_host.numel() * 2},

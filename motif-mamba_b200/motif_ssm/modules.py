@@ -354,3 +354,38 @@ def shard_model_tp(model, rank, world, group=None):
     for layer in model.backbone.layers:
         layer.mixer = TPMambamotif.from_full(layer.mixer, rank, world, group)
     return model
+
+
+class GraphedDecoder:
+    """One decode step of a MambaLMHeadModel captured as a CUDA graph.
+
+    Decode runs ~a dozen small kernels per layer (in_proj, conv update, x_proj, dt_proj,
+    state update, out_proj, norms), so it is launch-bound; replaying a captured graph
+    issues the whole step at once.  The cache tensors of `params` and the token buffer are
+    captured by address: feed tokens with ``step(tokens)``, which copies them into the
+    static buffer, replays, and returns the static logits buffer (valid until the next step).
+    """
+
+    def __init__(self, model, params, batch, warmup=2):
+        self.model, self.params = model, params
+        dev = model.lm_head.weight.device
+        self.tokens = torch.zeros(batch, 1, dtype=torch.long, device=dev)
+        snapshot = {k: (a.clone(), b.clone()) for k, (a, b) in params.key_value_memory_dict.items()}
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s), torch.no_grad():
+            for _ in range(warmup):
+                model(self.tokens, inference_params=params, num_last_tokens=1)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph), torch.no_grad():
+            self.logits = model(self.tokens, inference_params=params, num_last_tokens=1)
+        for k, (a, b) in snapshot.items():  # undo the state changes of warm-up and capture
+            params.key_value_memory_dict[k][0].copy_(a)
+            params.key_value_memory_dict[k][1].copy_(b)
+
+    def step(self, tokens):
+        self.tokens.copy_(tokens)
+        self.graph.replay()
+        self.params.seqlen_offset += 1
+        return self.logits

@@ -110,3 +110,23 @@ def test_lm_stack_backward_runs_bf16():
     loss.backward()
     for n, p in model.named_parameters():
         assert p.grad is not None and torch.isfinite(p.grad).all(), n
+
+
+def test_graphed_decode_matches_eager_decode():
+    from motif_ssm.modules import GraphedDecoder, InferenceParams, MambaConfig, MambaLMHeadModel
+    torch.manual_seed(3)
+    cfg = MambaConfig(d_model=128, n_layer=3, vocab_size=96, ssm_cfg={"d_state": 16})
+    model = MambaLMHeadModel(cfg, device=DEV, dtype=torch.bfloat16)
+    ids = torch.randint(0, 96, (4, 50), device=DEV)
+    with torch.no_grad():
+        pe = InferenceParams(max_seqlen=60, max_batch_size=4)
+        pg = InferenceParams(max_seqlen=60, max_batch_size=4)
+        model(ids[:, :40], inference_params=pe, num_last_tokens=1)
+        model(ids[:, :40], inference_params=pg, num_last_tokens=1)
+        pe.seqlen_offset = pg.seqlen_offset = 40
+        dec = GraphedDecoder(model, pg, batch=4)
+        for t in range(40, 50):
+            eager = model(ids[:, t:t + 1], inference_params=pe, num_last_tokens=1)
+            pe.seqlen_offset += 1
+            graphed = dec.step(ids[:, t:t + 1])
+            assert torch.equal(graphed, eager), t
