@@ -122,7 +122,8 @@ BwdShape bwd_shape(const ss_bwd_args *a) {
     s.tiles_per_group = (int)((dpg + cpg * s.kgroups - 1) / (cpg * s.kgroups));
     s.lpitch = round_up(a->seqlen, 4);
     s.acc_bytes = round_up(a->batch * a->n_groups * a->dstate * s.lpitch * 4, 256);
-    s.dh_bytes = 0;
+    // dstate > 16: fp32 per-step partial sums over states, carried between state blocks
+    s.dh_bytes = a->dstate > 16 ? round_up(rows * 2 * s.lpitch * 4, 256) : 0;
     return s;
 }
 
@@ -255,6 +256,7 @@ int ss_bwd(const ss_bwd_args *a, void *stream) {
     p.dz_bs = a->dz_bs; p.dz_ds = a->dz_ds; p.out_z_bs = a->out_z_bs; p.out_z_ds = a->out_z_ds;
     p.dA = a->dA; p.dD = a->dD; p.ddelta_bias = a->ddelta_bias;
     p.acc_dB = acc_dB; p.acc_dC = acc_dC;
+    p.s12 = s.dh_bytes > 0 ? reinterpret_cast<float *>(ws + 2 * s.acc_bytes) : nullptr;
     bool aligned = al16(a->u) && al16(a->delta) && al16(a->B) && al16(a->C) && al16(a->dout) &&
                    al16(a->du) && al16(a->ddelta) && st16(a->u_bs, es) && st16(a->u_ds, es) &&
                    st16(a->delta_bs, es) && st16(a->delta_ds, es) && st16(a->B_bs, es) && st16(a->B_gs, es) &&
@@ -268,8 +270,15 @@ int ss_bwd(const ss_bwd_args *a, void *stream) {
     if (a->recompute_out_z)
         aligned = aligned && al16(a->out_z) && st16(a->out_z_bs, es) && st16(a->out_z_ds, es);
     p.aligned = aligned ? 1 : 0;
-    e = launch_ss_bwd(p, a->itype, a->z != nullptr, st);
-    if (e != cudaSuccess) return cuda_fail(e, "ss_bwd launch");
+    // one launch per block of 16 states (a single launch for dstate <= 16)
+    for (int lo = 0; lo < (int)a->dstate; lo += 16) {
+        p.state_lo = lo;
+        p.nblk = (int)std::min<int64_t>(16, a->dstate - lo);
+        p.blk_first = lo == 0;
+        p.blk_last = lo + 16 >= a->dstate;
+        e = launch_ss_bwd(p, a->itype, a->z != nullptr, st);
+        if (e != cudaSuccess) return cuda_fail(e, "ss_bwd launch");
+    }
     const int64_t rows = a->batch * a->n_groups * a->dstate;
     if ((e = launch_acc_to_out(acc_dB, s.lpitch, a->dB, a->itype, rows, a->seqlen, st)) != cudaSuccess)
         return cuda_fail(e, "ss_bwd dB convert");

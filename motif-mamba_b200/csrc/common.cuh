@@ -14,7 +14,7 @@ namespace mss {
 
 constexpr int kChunkLen = 256;     // timesteps per x chunk (ss_chunk_len)
 constexpr int kMaxDstate = 64;     // largest dstate the forward accepts
-constexpr int kMaxDstateBwd = 16;  // largest dstate the backward accepts
+constexpr int kMaxDstateBwd = 64;  // largest dstate the backward accepts (blocks of 16)
 constexpr float kLog2e = 1.4426950408889634f;
 
 // ---- scalar conversions ------------------------------------------------------------

@@ -42,6 +42,9 @@ struct BwdParams {
     int64_t du_bs, du_ds, ddelta_bs, ddelta_ds, dz_bs, dz_ds, out_z_bs, out_z_ds;
     float *dA, *dD, *ddelta_bias;
     float *acc_dB, *acc_dC;  // fp32 accumulators (batch, n_groups, dstate, lpitch)
+    int state_lo, nblk;      // this launch's block of states [state_lo, state_lo + nblk), nblk <= 16
+    int blk_first, blk_last; // first / last block of the launch sequence
+    float *s12;              // dstate > 16: per-step partial sums over states (batch, dim, 2, lpitch)
 };
 
 // Sets the text ss_last_error() reports on this thread and returns `code`.

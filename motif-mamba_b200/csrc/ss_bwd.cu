@@ -170,8 +170,9 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
         for (int i = tid; i < 2 * NS * 32; i += NT) {
             const int q = i / (NS * 32), rem = i - q * NS * 32, n = rem >> 5, l = rem & 31;
             float v[8];
-            if (n < p.dstate) {
-                const T *row = (q == 0 ? gB + (int64_t)n * p.B_ns : gC + (int64_t)n * p.C_ns);
+            if (n < p.nblk) {
+                const int ng = p.state_lo + n;
+                const T *row = (q == 0 ? gB + (int64_t)ng * p.B_ns : gC + (int64_t)ng * p.C_ns);
                 load_items(row, kt0 + l * 8, L, vec, v);
             } else {
 #pragma unroll
@@ -234,7 +235,7 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
                         ozv[i] = ov[i] * silu;
                         dog[i] *= silu;
                     }
-                    if (valid) {
+                    if (valid && p.blk_first) {
                         store_items(reinterpret_cast<T *>(p.dz) + (int64_t)b * p.dz_bs + (int64_t)d * p.dz_ds, t0, L,
                                     vec, dzv);
                         if (p.recompute_out_z)
@@ -262,10 +263,11 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
             // A row and the chunk-start states of this channel, read once per pass (off the
             // per-state dependency chain)
             if (lane < NS) {  // states >= dstate read as zero (A, state), like their zero B / C rows
-                const bool st = valid && lane < p.dstate;
-                S.AX[w][0][lane] = st ? p.A[(int64_t)d * p.A_ds + (int64_t)lane * p.A_ns] : 0.f;
+                const bool st = valid && lane < p.nblk;
+                const int ng = p.state_lo + lane;
+                S.AX[w][0][lane] = st ? p.A[(int64_t)d * p.A_ds + (int64_t)ng * p.A_ns] : 0.f;
                 S.AX[w][1][lane] =
-                    (k > 0 && st) ? p.x[(row * p.n_chunks + (k - 1)) * 2 * p.dstate + 2 * lane + 1] : 0.f;
+                    (k > 0 && st) ? p.x[(row * p.n_chunks + (k - 1)) * 2 * p.dstate + 2 * ng + 1] : 0.f;
             }
             __syncwarp();
 
@@ -273,8 +275,8 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
             // has two independent dependency chains in flight.  An odd dstate pads the last
             // pair with a state whose A, B and C are zero (it contributes nothing).
 #pragma unroll 1
-            for (int n0 = 0; n0 < p.dstate; n0 += 2) {  // uniform over the CTA
-                const bool has1 = n0 + 1 < p.dstate;
+            for (int n0 = 0; n0 < p.nblk; n0 += 2) {  // uniform over the CTA
+                const bool has1 = n0 + 1 < p.nblk;
                 float An[2], A2[2], Pl[2];
                 f32x2 A2p[2], Anp[2];
                 f32x2 Bv[2][4], b2[2][4];
@@ -446,6 +448,35 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
             {
                 const float Dv = p.D ? p.D[(int64_t)d * p.D_s] : 0.f;
                 float du[8], dd[8], dDp = 0.f, dbp = 0.f;
+                if (p.s12 != nullptr) {
+                    // dstate > 16: this launch covers one block of 16 states; the per-step sums
+                    // over states are carried between launches in an fp32 scratch (pitch lpitch)
+                    float *r1 = p.s12 + ((int64_t)b * p.dim + d) * 2 * p.lpitch;
+                    float *r2 = r1 + p.lpitch;
+                    if (!p.blk_first) {
+                        float a1[8], a2[8];
+                        load_items(r1, t0, L, vec, a1);
+                        load_items(r2, t0, L, vec, a2);
+#pragma unroll
+                        for (int m = 0; m < 4; ++m) {
+                            S1[m] = add2(S1[m], pack2(a1[2 * m], a1[2 * m + 1]));
+                            S2[m] = add2(S2[m], pack2(a2[2 * m], a2[2 * m + 1]));
+                        }
+                    }
+                    if (!p.blk_last) {
+                        float a1[8], a2[8];
+#pragma unroll
+                        for (int m = 0; m < 4; ++m) {
+                            const float2 v1 = unpack2(S1[m]), v2 = unpack2(S2[m]);
+                            a1[2 * m] = v1.x; a1[2 * m + 1] = v1.y;
+                            a2[2 * m] = v2.x; a2[2 * m + 1] = v2.y;
+                        }
+                        if (valid) {
+                            store_items(r1, t0, L, vec, a1);
+                            store_items(r2, t0, L, vec, a2);
+                        }
+                    }
+                }
 #pragma unroll
                 for (int m = 0; m < 4; ++m) {
                     const float2 s1 = unpack2(S1[m]), s2 = unpack2(S2[m]), df = unpack2(dtf2[m]);
@@ -465,7 +496,7 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
                         }
                     }
                 }
-                if (valid) {
+                if (valid && p.blk_last) {
                     store_items(reinterpret_cast<T *>(p.du) + (int64_t)b * p.du_bs + (int64_t)d * p.du_ds, t0, L,
                                 vec, du);
                     store_items(reinterpret_cast<T *>(p.ddelta) + (int64_t)b * p.ddelta_bs + (int64_t)d * p.ddelta_ds,
@@ -491,9 +522,9 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
             const int n = rem / (CK / 4), pos = (rem - n * (CK / 4)) * 4;
             const int t = ((pos >> 2) & 31) * 8 + (pos >> 7) * 4;  // first timestep of this 4-group
             float *src = &S.ACC[q][n][pos];
-            if (n < p.dstate && t < clen) {
+            if (n < p.nblk && t < clen) {
                 float *dst = (q == 0 ? p.acc_dB : p.acc_dC) +
-                             (((int64_t)b * p.n_groups + g) * p.dstate + n) * p.lpitch + kt0 + t;
+                             (((int64_t)b * p.n_groups + g) * p.dstate + p.state_lo + n) * p.lpitch + kt0 + t;
                 red_add_v4(dst, src[0], src[1], src[2], src[3]);
             }
             src[0] = src[1] = src[2] = src[3] = 0.f;
@@ -503,15 +534,15 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
     for (int i = tid; i < K * W * NS; i += NT) {
         const int cg = i / (W * NS), rem = i - cg * W * NS, ww = rem / NS, n = rem - ww * NS;
         const int cin = (tile * K + cg) * W + ww;
-        if (cin < p.dpg && n < p.dstate)
-            atomicAdd(p.dA + (int64_t)(g * p.dpg + cin) * p.dstate + n, S.DAACC[cg][ww][n]);
+        if (cin < p.dpg && n < p.nblk)
+            atomicAdd(p.dA + (int64_t)(g * p.dpg + cin) * p.dstate + p.state_lo + n, S.DAACC[cg][ww][n]);
     }
     for (int i = tid; i < K * W; i += NT) {
         const int cg = i / W, ww = i - cg * W;
         const int cin = (tile * K + cg) * W + ww;
         if (cin < p.dpg) {
-            if (p.dD) atomicAdd(p.dD + g * p.dpg + cin, S.PBD[cg][ww][0]);
-            if (p.ddelta_bias) atomicAdd(p.ddelta_bias + g * p.dpg + cin, S.PBD[cg][ww][1]);
+            if (p.dD && p.blk_last) atomicAdd(p.dD + g * p.dpg + cin, S.PBD[cg][ww][0]);
+            if (p.ddelta_bias && p.blk_last) atomicAdd(p.ddelta_bias + g * p.dpg + cin, S.PBD[cg][ww][1]);
         }
     }
 }

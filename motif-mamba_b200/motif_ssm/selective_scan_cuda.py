@@ -8,7 +8,7 @@ allocates) and the work runs in ``libmotif_ssm.so`` on the current CUDA stream.
 Differences from the reference, all raising instead of silently diverging:
 * complex ``A`` and constant (2-D) ``B`` / ``C`` raise ``NotImplementedError``;
 * ``P`` / ``Q`` / ``gamma`` (the motif low-rank path) raise ``NotImplementedError``;
-* ``dstate`` above ``MAX_DSTATE`` (forward) or 16 (backward) raises;
+* ``dstate`` above ``MAX_DSTATE`` (64) raises (the reference allows 256);
 * ``x`` holds one (decay, state) pair per ``CHUNK_LEN`` = 256 steps instead of 2048;
   ``x[:, :, -1, 1::2]`` is still the final state and ``bwd`` expects this ``x``.
 """
