@@ -76,6 +76,11 @@ typedef struct {
     void *out_z;        int64_t out_z_bs, out_z_ds;    /* required iff z: out * silu(z) */
     float *x;           /* contiguous (batch, dim, n_chunks, 2*dstate) */
     void *workspace;    int64_t workspace_bytes;
+    /* motif low-rank coupling h += dt * P (Q h_prev) (selective_scan_interface.py:402-433);
+     * P == NULL disables it.  fp32 contiguous: P (dstate, r) and Q (r, dstate), or per channel
+     * P (dim, dstate, r) and Q (dim, r, dstate) when pq_per_dim; r = pq_rank <= 8, dstate <= 16. */
+    const float *P;     const float *Q;
+    int64_t pq_rank;    int32_t pq_per_dim; int32_t _pad_pq;
 } ss_fwd_args;
 
 typedef struct {
@@ -105,6 +110,9 @@ typedef struct {
     void *dz;           int64_t dz_bs, dz_ds;          /* required iff z */
     void *out_z;        int64_t out_z_bs, out_z_ds;    /* required iff recompute_out_z */
     void *workspace;    int64_t workspace_bytes;
+    const float *P;     const float *Q;                /* as in ss_fwd_args; NULL: no coupling */
+    int64_t pq_rank;    int32_t pq_per_dim; int32_t _pad_pq;
+    float *dP;          float *dQ;                     /* fp32, shapes of P and Q, overwritten */
 } ss_bwd_args;
 
 typedef struct {

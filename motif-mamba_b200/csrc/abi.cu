@@ -46,7 +46,7 @@ FwdShape fwd_shape(const ss_fwd_args *a) {
     FwdShape s{1, (int)a->seqlen, 0, 0};
     const int64_t rows = a->batch * a->dim;
     const int64_t target = (int64_t)kNumSMs * 512;  // resident threads wanted
-    if (rows > 0 && rows < target && a->seqlen > 2 * kChunkLen) {
+    if (!a->P && rows > 0 && rows < target && a->seqlen > 2 * kChunkLen) {
         int64_t want = (target + rows - 1) / rows;
         int64_t seg = round_up((a->seqlen + want - 1) / want, kChunkLen);
         int64_t n = (a->seqlen + seg - 1) / seg;
@@ -61,6 +61,15 @@ FwdShape fwd_shape(const ss_fwd_args *a) {
     return s;
 }
 
+// Motif coupling limits: P and Q both given, rank 1..8, dstate <= 16 (states in registers).
+int check_pq(const char *who, const float *P, const float *Q, int64_t rank, int64_t dstate) {
+    if (!P && !Q) return MSS_OK;
+    if (!P || !Q) return fail(MSS_ERR_INVALID, "%s: P and Q must be given together", who);
+    if (rank < 1 || rank > 8) return fail(MSS_ERR_UNSUPPORTED, "%s: pq_rank must be in [1, 8]", who);
+    if (dstate > 16) return fail(MSS_ERR_UNSUPPORTED, "%s: the P/Q coupling supports dstate <= 16", who);
+    return MSS_OK;
+}
+
 int check_fwd(const ss_fwd_args *a, bool need_ptrs = true) {
     if (!a) return fail(MSS_ERR_INVALID, "ss_fwd: null argument struct");
     if (!valid_type(a->itype)) return fail(MSS_ERR_INVALID, "ss_fwd: itype must be f32, f16 or bf16");
@@ -72,13 +81,13 @@ int check_fwd(const ss_fwd_args *a, bool need_ptrs = true) {
                     (long long)a->dstate, kMaxDstate);
     if (a->n_groups < 1 || (a->dim > 0 && a->dim % a->n_groups != 0))
         return fail(MSS_ERR_INVALID, "ss_fwd: n_groups must divide dim");
-    if (a->batch * a->dim * a->seqlen == 0 || !need_ptrs) return MSS_OK;
+    if (a->batch * a->dim * a->seqlen == 0 || !need_ptrs) return check_pq("ss_fwd", a->P, a->Q, a->pq_rank, a->dstate);
     if (!a->u || !a->delta || !a->A || !a->B || !a->C || !a->out || !a->x)
         return fail(MSS_ERR_INVALID, "ss_fwd: u, delta, A, B, C, out and x must be non-null");
     if (a->z && !a->out_z) return fail(MSS_ERR_INVALID, "ss_fwd: out_z must be given with z");
     if (a->seqlen > (int64_t)1 << 31 || a->dim > (int64_t)1 << 30)
         return fail(MSS_ERR_UNSUPPORTED, "ss_fwd: size out of range");
-    return MSS_OK;
+    return check_pq("ss_fwd", a->P, a->Q, a->pq_rank, a->dstate);
 }
 
 int check_bwd(const ss_bwd_args *a, bool need_ptrs = true) {
@@ -91,7 +100,7 @@ int check_bwd(const ss_bwd_args *a, bool need_ptrs = true) {
                     (long long)a->dstate, kMaxDstateBwd);
     if (a->n_groups < 1 || (a->dim > 0 && a->dim % a->n_groups != 0))
         return fail(MSS_ERR_INVALID, "ss_bwd: n_groups must divide dim");
-    if (!need_ptrs) return MSS_OK;
+    if (!need_ptrs) return check_pq("ss_bwd", a->P, a->Q, a->pq_rank, a->dstate);
     if (a->z && (!a->out || !a->dz)) return fail(MSS_ERR_INVALID, "ss_bwd: out and dz must be given with z");
     if (a->recompute_out_z && (!a->z || !a->out_z))
         return fail(MSS_ERR_INVALID, "ss_bwd: recompute_out_z needs z and out_z");
@@ -104,12 +113,13 @@ int check_bwd(const ss_bwd_args *a, bool need_ptrs = true) {
         return fail(MSS_ERR_INVALID, "ss_bwd: u, delta, A, B, C, dout, du, ddelta and x must be non-null");
     if (a->seqlen > (int64_t)1 << 31 || a->dim > (int64_t)1 << 30)
         return fail(MSS_ERR_UNSUPPORTED, "ss_bwd: size out of range");
-    return MSS_OK;
+    if (a->P && (!a->dP || !a->dQ)) return fail(MSS_ERR_INVALID, "ss_bwd: dP and dQ must be given with P");
+    return check_pq("ss_bwd", a->P, a->Q, a->pq_rank, a->dstate);
 }
 
 struct BwdShape {
     int kgroups, tiles_per_group;
-    int64_t lpitch, acc_bytes, dh_bytes;
+    int64_t lpitch, acc_bytes, dh_bytes, ckpt_bytes;
 };
 BwdShape bwd_shape(const ss_bwd_args *a) {
     BwdShape s;
@@ -124,6 +134,8 @@ BwdShape bwd_shape(const ss_bwd_args *a) {
     s.acc_bytes = round_up(a->batch * a->n_groups * a->dstate * s.lpitch * 4, 256);
     // dstate > 16: fp32 per-step partial sums over states, carried between state blocks
     s.dh_bytes = a->dstate > 16 ? round_up(rows * 2 * s.lpitch * 4, 256) : 0;
+    // P/Q coupling: the 16 states at every 16-step segment start
+    s.ckpt_bytes = a->P ? round_up(rows * ((a->seqlen + 15) / 16) * 16 * 4, 256) : 0;
     return s;
 }
 
@@ -192,7 +204,13 @@ int ss_fwd(const ss_fwd_args *a, void *stream) {
         aligned = aligned && al16(a->z) && al16(a->out_z) && st16(a->z_bs, es) && st16(a->z_ds, es) &&
                   st16(a->out_z_bs, es) && st16(a->out_z_ds, es);
     p.aligned = aligned ? 1 : 0;
-    cudaError_t e = launch_ss_fwd(p, a->itype, a->z != nullptr, static_cast<cudaStream_t>(stream));
+    cudaError_t e;
+    if (a->P) {
+        p.P = a->P; p.Q = a->Q; p.pq_rank = (int)a->pq_rank; p.pq_per_dim = a->pq_per_dim ? 1 : 0;
+        e = launch_ss_fwd_pq(p, a->itype, a->z != nullptr, static_cast<cudaStream_t>(stream));
+    } else {
+        e = launch_ss_fwd(p, a->itype, a->z != nullptr, static_cast<cudaStream_t>(stream));
+    }
     if (e != cudaSuccess) return cuda_fail(e, "ss_fwd launch");
     return MSS_OK;
 }
@@ -202,7 +220,7 @@ int ss_bwd_workspace_size(const ss_bwd_args *a, int64_t *bytes) {
     if (rc) return rc;
     if (!bytes) return fail(MSS_ERR_INVALID, "ss_bwd_workspace_size: null output");
     BwdShape s = bwd_shape(a);
-    *bytes = 2 * s.acc_bytes + s.dh_bytes;
+    *bytes = 2 * s.acc_bytes + s.dh_bytes + s.ckpt_bytes;
     return MSS_OK;
 }
 
@@ -218,6 +236,11 @@ int ss_bwd(const ss_bwd_args *a, void *stream) {
     if (a->dD && (e = cudaMemsetAsync(a->dD, 0, a->dim * 4, st)) != cudaSuccess) return cuda_fail(e, "ss_bwd memset dD");
     if (a->ddelta_bias && (e = cudaMemsetAsync(a->ddelta_bias, 0, a->dim * 4, st)) != cudaSuccess)
         return cuda_fail(e, "ss_bwd memset ddelta_bias");
+    if (a->P) {
+        const int64_t np = (a->pq_per_dim ? a->dim : 1) * a->dstate * a->pq_rank * 4;
+        if ((e = cudaMemsetAsync(a->dP, 0, np, st)) != cudaSuccess) return cuda_fail(e, "ss_bwd memset dP");
+        if ((e = cudaMemsetAsync(a->dQ, 0, np, st)) != cudaSuccess) return cuda_fail(e, "ss_bwd memset dQ");
+    }
     if (a->batch * a->dim * a->seqlen == 0) {
         const int64_t nbc = a->batch * a->n_groups * a->dstate * a->seqlen * es;
         if (nbc > 0) {
@@ -227,7 +250,7 @@ int ss_bwd(const ss_bwd_args *a, void *stream) {
         return MSS_OK;
     }
     BwdShape s = bwd_shape(a);
-    const int64_t need = 2 * s.acc_bytes + s.dh_bytes;
+    const int64_t need = 2 * s.acc_bytes + s.dh_bytes + s.ckpt_bytes;
     if (!a->workspace || a->workspace_bytes < need)
         return fail(MSS_ERR_WORKSPACE, "ss_bwd: workspace of %lld bytes required", (long long)need);
     if (!al16(a->workspace)) return fail(MSS_ERR_ALIGNMENT, "ss_bwd: workspace must be 16-byte aligned");
@@ -270,8 +293,15 @@ int ss_bwd(const ss_bwd_args *a, void *stream) {
     if (a->recompute_out_z)
         aligned = aligned && al16(a->out_z) && st16(a->out_z_bs, es) && st16(a->out_z_ds, es);
     p.aligned = aligned ? 1 : 0;
+    if (a->P) {
+        p.P = a->P; p.Q = a->Q; p.pq_rank = (int)a->pq_rank; p.pq_per_dim = a->pq_per_dim ? 1 : 0;
+        p.dP = a->dP; p.dQ = a->dQ;
+        p.ckpt = reinterpret_cast<float *>(ws + 2 * s.acc_bytes + s.dh_bytes);
+        e = launch_ss_bwd_pq(p, a->itype, a->z != nullptr, st);
+        if (e != cudaSuccess) return cuda_fail(e, "ss_bwd launch");
+    }
     // one launch per block of 16 states (a single launch for dstate <= 16)
-    for (int lo = 0; lo < (int)a->dstate; lo += 16) {
+    for (int lo = 0; !a->P && lo < (int)a->dstate; lo += 16) {
         p.state_lo = lo;
         p.nblk = (int)std::min<int64_t>(16, a->dstate - lo);
         p.blk_first = lo == 0;

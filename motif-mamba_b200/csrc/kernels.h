@@ -22,6 +22,8 @@ struct FwdParams {
     int64_t delta_bias_s;
     float *x;
     float *ws_h, *ws_dts;  // segment carries (n_seg > 1)
+    const float *P, *Q;    // motif coupling (nullptr: none)
+    int pq_rank, pq_per_dim;
 };
 
 struct BwdParams {
@@ -45,6 +47,10 @@ struct BwdParams {
     int state_lo, nblk;      // this launch's block of states [state_lo, state_lo + nblk), nblk <= 16
     int blk_first, blk_last; // first / last block of the launch sequence
     float *s12;              // dstate > 16: per-step partial sums over states (batch, dim, 2, lpitch)
+    const float *P, *Q;      // motif coupling (nullptr: none)
+    int pq_rank, pq_per_dim;
+    float *dP, *dQ;
+    float *ckpt;             // motif backward: states every 16 steps (batch, dim, ceil(L/16), 16)
 };
 
 // Sets the text ss_last_error() reports on this thread and returns `code`.
@@ -61,6 +67,8 @@ cudaError_t launch_conv1d_fwd(const conv1d_args &a, bool vec, cudaStream_t st);
 cudaError_t launch_conv1d_bwd(const conv1d_args &a, bool vec, cudaStream_t st);
 cudaError_t launch_conv1d_update(const conv1d_update_args &a, cudaStream_t st);
 cudaError_t launch_state_update(const ssm_state_update_args &a, cudaStream_t st);
+cudaError_t launch_ss_fwd_pq(const FwdParams &p, int itype, bool has_z, cudaStream_t st);
+cudaError_t launch_ss_bwd_pq(const BwdParams &p, int itype, bool has_z, cudaStream_t st);
 cudaError_t launch_acc_to_out(const float *acc, int64_t lpitch, void *out, int itype, int64_t rows,
                               int64_t seqlen, cudaStream_t st);
 

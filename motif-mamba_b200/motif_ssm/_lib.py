@@ -35,6 +35,8 @@ class SsFwdArgs(ctypes.Structure):
         ("out_z", vp), ("out_z_bs", i64), ("out_z_ds", i64),
         ("x", vp),
         ("workspace", vp), ("workspace_bytes", i64),
+        ("P", vp), ("Q", vp),
+        ("pq_rank", i64), ("pq_per_dim", i32), ("_pad_pq", i32),
     ]
 
 
@@ -59,6 +61,9 @@ class SsBwdArgs(ctypes.Structure):
         ("dz", vp), ("dz_bs", i64), ("dz_ds", i64),
         ("out_z", vp), ("out_z_bs", i64), ("out_z_ds", i64),
         ("workspace", vp), ("workspace_bytes", i64),
+        ("P", vp), ("Q", vp),
+        ("pq_rank", i64), ("pq_per_dim", i32), ("_pad_pq", i32),
+        ("dP", vp), ("dQ", vp),
     ]
 
 

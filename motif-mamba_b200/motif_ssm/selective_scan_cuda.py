@@ -7,7 +7,9 @@ allocates) and the work runs in ``libmotif_ssm.so`` on the current CUDA stream.
 
 Differences from the reference, all raising instead of silently diverging:
 * complex ``A`` and constant (2-D) ``B`` / ``C`` raise ``NotImplementedError``;
-* ``P`` / ``Q`` / ``gamma`` (the motif low-rank path) raise ``NotImplementedError``;
+* ``P`` / ``Q`` (the motif low-rank coupling, ``:342-369``) must be contiguous fp32 with
+  ``dstate <= 16`` (the reference allows 256); ``gamma`` is checked and, as in the
+  reference's dense P/Q kernels, not used;
 * ``dstate`` above ``MAX_DSTATE`` (64) raises (the reference allows 256);
 * ``x`` holds one (decay, state) pair per ``CHUNK_LEN`` = 256 steps instead of 2048;
   ``x[:, :, -1, 1::2]`` is still the final state and ``bwd`` expects this ``x``.
@@ -48,9 +50,42 @@ def _check_shape(t, *shape, name="tensor"):
     _req(tuple(t.shape) == tuple(shape), f"{name} must have shape {tuple(shape)}, got {tuple(t.shape)}")
 
 
+def _check_pq(P, Q, gamma, dim, dstate):
+    """Shape rules of the reference binding (``selective_scan.cpp:342-369``)."""
+    _req(P is None or Q is not None, "Q must be provided when P is provided")
+    _req(Q is None or P is not None, "P must be provided when Q is provided")
+    if P is not None:
+        _req(P.is_cuda and Q.is_cuda, "P and Q must be CUDA tensors")
+        _req(P.dim() == Q.dim() and P.dim() in (2, 3), "P/Q must be 2D or 3D with same rank")
+        if P.dim() == 2:
+            _req(P.size(0) == dstate and Q.size(1) == dstate and P.size(1) == Q.size(0),
+                 "Expect P(dstate, r), Q(r, dstate)")
+        else:
+            _req(P.size(0) == dim and Q.size(0) == dim, "P/Q dim mismatch")
+            _req(P.size(1) == dstate and Q.size(2) == dstate and P.size(2) == Q.size(1),
+                 "Expect P(dim, dstate, r), Q(dim, r, dstate)")
+        _req(P.size(-1) <= 8, "Current dense CUDA forward supports pq_rank <= 8")
+        _req(P.dtype == torch.float32 and Q.dtype == torch.float32, "P and Q must be float32")
+        _req(P.is_contiguous() and Q.is_contiguous(), "P and Q must be contiguous")
+        if dstate > 16:
+            raise NotImplementedError("selective_scan_cuda: the P/Q coupling supports dstate <= 16 in this library")
+    if gamma is not None:
+        _req(gamma.is_cuda, "gamma must be CUDA tensor")
+        _req(gamma.dim() in (1, 2), "gamma must be 1D or 2D")
+        if gamma.dim() == 1:
+            _req(gamma.size(0) == dstate, "gamma(1D) shape must be (dstate,)")
+        else:
+            _req(gamma.size(0) == dim and gamma.size(1) == dstate, "gamma(2D) shape must be (dim, dstate)")
+
+
+def _fill_pq(a, P, Q):
+    if P is not None:
+        a.P, a.Q = _ptr(P), _ptr(Q)
+        a.pq_rank = P.size(-1)
+        a.pq_per_dim = 1 if P.dim() == 3 else 0
+
+
 def _check_common(u, delta, A, B, C, D, z, delta_bias, P, Q, gamma):
-    if P is not None or Q is not None or gamma is not None:
-        raise NotImplementedError("selective_scan_cuda: the P/Q (motif low-rank) path is not built in this library")
     if A.is_complex():
         raise NotImplementedError("selective_scan_cuda: complex A is not supported by this library")
     _req(u.dtype in _ITYPE, "u must be float32, float16 or bfloat16")
@@ -85,6 +120,7 @@ def _check_common(u, delta, A, B, C, D, z, delta_bias, P, Q, gamma):
         _req(z.is_cuda, "z must be a CUDA tensor")
         _req(z.stride(-1) == 1 or z.size(-1) == 1, "z must have unit stride in the last dimension")
         _check_shape(z, batch, dim, seqlen, name="z")
+    _check_pq(P, Q, gamma, dim, dstate)
     return batch, dim, seqlen, dstate, n_groups
 
 
@@ -120,6 +156,7 @@ def fwd(u, delta, A, B, C, D=None, z=None, delta_bias=None, P=None, Q=None, gamm
     out_z = torch.empty_like(z) if z is not None else None
     a = _lib.SsFwdArgs()
     _fill_common(a, u, delta, A, B, C, D, z, delta_bias, sizes, delta_softplus)
+    _fill_pq(a, P, Q)
     a.out, a.out_bs, a.out_ds = _ptr(out), out.stride(0), out.stride(1)
     if z is not None:
         a.out_z, a.out_z_bs, a.out_z_ds = _ptr(out_z), out_z.stride(0), out_z.stride(1)
@@ -142,10 +179,11 @@ def bwd(u, delta, A, B, C, D=None, z=None, delta_bias=None, P=None, Q=None, gamm
 
     Returns ``[du, ddelta, dA, dB, dC, dD, ddelta_bias]`` plus ``dz`` when ``z`` is
     given plus ``out_z`` when ``recompute_out_z``.  A caller-provided ``dz`` is written
-    in place (``selective_scan_interface.py:593-603`` passes a view into ``dxz``).
+    in place (``selective_scan_interface.py:593-603`` passes a view into ``dxz``).  With
+    ``P`` / ``Q`` the gradients of the coupling go to ``dP_out`` / ``dQ_out`` (fp32, the
+    shapes of P and Q, overwritten; allocated and dropped when not given), as in
+    ``selective_scan.cpp:579-590``.
     """
-    if dP_out is not None or dQ_out is not None:
-        raise NotImplementedError("selective_scan_cuda: the P/Q (motif low-rank) path is not built in this library")
     sizes = _check_common(u, delta, A, B, C, D, z, delta_bias, P, Q, gamma)
     batch, dim, seqlen, dstate, n_groups = sizes
     _req(dout is not None, "dout must be given")
@@ -158,7 +196,7 @@ def bwd(u, delta, A, B, C, D=None, z=None, delta_bias=None, P=None, Q=None, gamm
         _req(tuple(x.shape) == (batch, dim, nc, 2 * dstate),
              f"x must have shape {(batch, dim, nc, 2 * dstate)} (chunk length {CHUNK_LEN}), got {tuple(x.shape)}")
     else:
-        _req(nc <= 1, "x (the forward's chunk states) is required when seqlen > %d" % CHUNK_LEN)
+        _req(nc <= 1 or P is not None, "x (the forward's chunk states) is required when seqlen > %d" % CHUNK_LEN)
     if z is not None:
         _req(out is not None, "out must be given with z")
         _req(out.dtype == u.dtype and out.is_cuda, "out must be a CUDA tensor with the dtype of u")
@@ -178,16 +216,27 @@ def bwd(u, delta, A, B, C, D=None, z=None, delta_bias=None, P=None, Q=None, gamm
     dD = torch.empty_like(D) if D is not None else None
     ddelta_bias = torch.empty_like(delta_bias) if delta_bias is not None else None
     out_z = torch.empty_like(out) if (recompute_out_z and z is not None) else None
+    if P is not None:
+        dP_out = torch.empty_like(P) if dP_out is None else dP_out
+        dQ_out = torch.empty_like(Q) if dQ_out is None else dQ_out
+        _req(dP_out.is_cuda and dQ_out.is_cuda, "dP_out and dQ_out must be CUDA tensors")
+        _req(dP_out.dtype == torch.float32 and dQ_out.dtype == torch.float32, "dP_out and dQ_out must be float32")
+        _req(dP_out.shape == P.shape, "dP_out shape mismatch")
+        _req(dQ_out.shape == Q.shape, "dQ_out shape mismatch")
+        _req(dP_out.is_contiguous() and dQ_out.is_contiguous(), "dP_out and dQ_out must be contiguous")
 
     a = _lib.SsBwdArgs()
     _fill_common(a, u, delta, A, B, C, D, z, delta_bias, sizes, delta_softplus)
     a.recompute_out_z = 1 if out_z is not None else 0
+    _fill_pq(a, P, Q)
+    if P is not None:
+        a.dP, a.dQ = _ptr(dP_out), _ptr(dQ_out)
     if z is not None:
         a.out, a.out_bs, a.out_ds = _ptr(out), out.stride(0), out.stride(1)
         a.dz, a.dz_bs, a.dz_ds = _ptr(dz), dz.stride(0), dz.stride(1)
     if out_z is not None:
         a.out_z, a.out_z_bs, a.out_z_ds = _ptr(out_z), out_z.stride(0), out_z.stride(1)
-    a.x = _ptr(x) if x is not None else _ptr(u)  # never read when seqlen <= CHUNK_LEN
+    a.x = _ptr(x) if x is not None else _ptr(u)  # never read when seqlen <= CHUNK_LEN or with P
     a.dout, a.dout_bs, a.dout_ds = _ptr(dout), dout.stride(0), dout.stride(1)
     a.du, a.du_bs, a.du_ds = _ptr(du), du.stride(0), du.stride(1)
     a.ddelta, a.ddelta_bs, a.ddelta_ds = _ptr(ddelta), ddelta.stride(0), ddelta.stride(1)

@@ -76,12 +76,72 @@ class SelectiveScanFn(torch.autograd.Function):
                 ddelta_bias if delta_bias is not None else None, None, None)
 
 
+class SelectiveScanPQFn(torch.autograd.Function):
+    """The scan with the motif low-rank coupling ``h += dt * P (Q h_prev)``
+    (``selective_scan_interface.py:94-219``).  Unlike the reference's dense kernel this one
+    also takes ``z`` (the reference sends that case to its per-step torch loop,
+    ``:262-350``), and ``dP`` / ``dQ`` are the exact gradients from the backward kernel (the
+    reference's default recomputes them by autograd through that loop).  ``gamma`` is
+    accepted and unused, as in the reference's forward."""
+
+    @staticmethod
+    def forward(ctx, u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softplus=False,
+                return_last_state=False, P=None, Q=None, gamma=None):
+        if A.is_complex():
+            raise NotImplementedError("P/Q path supports real A only")
+        if P is None or Q is None:
+            raise ValueError("P and Q must both be provided")
+        if gamma is not None and gamma.requires_grad:
+            raise NotImplementedError("the P/Q backward does not return dgamma")
+        u, delta, B, C, z = (_last_dim_contig(t) for t in (u, delta, B, C, z))
+        if D is not None:
+            D = D.contiguous()
+        ctx.squeeze_B = B.dim() == 3
+        ctx.squeeze_C = C.dim() == 3
+        if ctx.squeeze_B:
+            B = B.unsqueeze(1)
+        if ctx.squeeze_C:
+            C = C.unsqueeze(1)
+        ctx.P_dtype, ctx.Q_dtype = P.dtype, Q.dtype
+        P32 = P.detach().float().contiguous()
+        Q32 = Q.detach().float().contiguous()
+        out, x, *rest = selective_scan_cuda.fwd(u, delta, A, B, C, D=D, z=z, delta_bias=delta_bias,
+                                                P=P32, Q=Q32, gamma=gamma, delta_softplus=delta_softplus)
+        ctx.delta_softplus = delta_softplus
+        ctx.has_z = z is not None
+        ctx.save_for_backward(u, delta, A, B, C, D, z, delta_bias, P32, Q32, out if ctx.has_z else None)
+        last_state = x[:, :, -1, 1::2]
+        ctx.mark_non_differentiable(last_state)
+        result = rest[0] if ctx.has_z else out
+        return (result, last_state) if return_last_state else result
+
+    @staticmethod
+    def backward(ctx, dout, *unused):
+        u, delta, A, B, C, D, z, delta_bias, P32, Q32, out = ctx.saved_tensors
+        dout = _last_dim_contig(dout)
+        dP = torch.empty_like(P32)
+        dQ = torch.empty_like(Q32)
+        du, ddelta, dA, dB, dC, dD, ddelta_bias, *rest = selective_scan_cuda.bwd(
+            u, delta, A, B, C, D=D, z=z, delta_bias=delta_bias, P=P32, Q=Q32, dout=dout, x=None, out=out,
+            dz=None, dP_out=dP, dQ_out=dQ, delta_softplus=ctx.delta_softplus, recompute_out_z=False)
+        dz = rest[0] if ctx.has_z else None
+        if ctx.squeeze_B:
+            dB = dB.squeeze(1)
+        if ctx.squeeze_C:
+            dC = dC.squeeze(1)
+        return (du, ddelta, dA, dB, dC, dD if D is not None else None, dz,
+                ddelta_bias if delta_bias is not None else None, None, None,
+                dP.to(ctx.P_dtype), dQ.to(ctx.Q_dtype), None)
+
+
 def selective_scan_fn(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softplus=False,
                       return_last_state=False, P=None, Q=None, gamma=None):
     """If ``return_last_state`` is True returns ``(out, last_state)``; ``last_state`` is
-    (batch, dim, dstate) and receives no gradient."""
+    (batch, dim, dstate) and receives no gradient.  ``P`` / ``Q`` switch on the motif
+    low-rank coupling (``selective_scan_interface.py:237-259``)."""
     if P is not None or Q is not None or gamma is not None:
-        raise NotImplementedError("selective_scan_fn: the P/Q (motif low-rank) path is not built in this library")
+        return SelectiveScanPQFn.apply(u, delta, A, B, C, D, z, delta_bias, delta_softplus, return_last_state,
+                                       P, Q, gamma)
     return SelectiveScanFn.apply(u, delta, A, B, C, D, z, delta_bias, delta_softplus, return_last_state)
 
 

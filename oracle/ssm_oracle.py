@@ -37,7 +37,7 @@ def _softplus(x):
 
 
 def selective_scan_ref(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softplus=False,
-                       return_last_state=False):
+                       return_last_state=False, P=None, Q=None, gamma=None):
     """Sequential diagonal SSM scan, real A only.
 
     h_t = exp(delta_t * A) * h_{t-1} + delta_t * B_t * u_t ;  y_t = <C_t, h_t>
@@ -73,8 +73,22 @@ def selective_scan_ref(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta
         dBu = (delta * u).unsqueeze(-1) * B.permute(0, 1, 3, 2)
     h = u.new_zeros(batch, dim, dstate)
     ys = []
+    use_pq = P is not None or Q is not None
+    if use_pq:
+        # motif low-rank coupling (selective_scan_interface.py:402-433): gamma is not used there
+        if P is None or Q is None:
+            raise ValueError("P and Q must be both provided")
+        if P.dim() == 2:
+            Pd, Qd = P.float().unsqueeze(0).expand(dim, -1, -1), Q.float().unsqueeze(0).expand(dim, -1, -1)
+        else:
+            Pd, Qd = P.float(), Q.float()
     for i in range(u.shape[2]):
-        h = dA[:, :, i] * h + dBu[:, :, i]
+        if use_pq:
+            q = torch.einsum("drn,bdn->bdr", Qd, h)
+            pq = torch.einsum("dnr,bdr->bdn", Pd, q)
+            h = dA[:, :, i] * h + delta[:, :, i].unsqueeze(-1) * pq + dBu[:, :, i]
+        else:
+            h = dA[:, :, i] * h + dBu[:, :, i]
         if not var_C:
             y = (h * C.unsqueeze(0)).sum(-1)
         elif C.dim() == 3:
@@ -181,13 +195,15 @@ def rms_norm_ref(x, weight, eps=1e-5):
 
 
 def scan_with_grads(inputs, dout, delta_softplus, return_last_state=True):
-    """Run ``selective_scan_ref`` with autograd; returns (out, last_state, grads dict)."""
+    """Run ``selective_scan_ref`` with autograd; returns (out, last_state, grads dict).
+    ``inputs`` may carry ``P`` / ``Q`` (motif path)."""
     leaves = {k: (v.detach().clone().requires_grad_(True) if v is not None else None)
               for k, v in inputs.items()}
     out, last = selective_scan_ref(leaves["u"], leaves["delta"], leaves["A"], leaves["B"],
                                    leaves["C"], leaves["D"], z=leaves["z"],
                                    delta_bias=leaves["delta_bias"],
-                                   delta_softplus=delta_softplus, return_last_state=True)
+                                   delta_softplus=delta_softplus, return_last_state=True,
+                                   P=leaves.get("P"), Q=leaves.get("Q"))
     out.backward(dout)
     grads = {k: (v.grad if v is not None else None) for k, v in leaves.items()}
     return out.detach(), last.detach(), grads

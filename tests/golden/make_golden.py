@@ -83,7 +83,8 @@ def load_reference():
 
 
 def scan_case(ssi, name, *, batch, dim, seqlen, dstate, dtype=torch.float32, groups=0,
-              has_z=True, has_D=True, has_bias=True, softplus=True, grads=True, seed=0):
+              has_z=True, has_D=True, has_bias=True, softplus=True, grads=True, seed=0, pq_rank=0,
+              pq_per_dim=False):
     """Inputs distributed as BASELINE config 0: N(0,1) data, S4D-real A, bias = inv-softplus(U[1e-3, 1e-1])."""
     g = torch.Generator().manual_seed(seed)
     u = torch.randn(batch, dim, seqlen, generator=g).to(dtype)
@@ -107,10 +108,19 @@ def scan_case(ssi, name, *, batch, dim, seqlen, dstate, dtype=torch.float32, gro
         delta_bias = None
     dout = torch.randn(batch, dim, seqlen, generator=g).to(dtype)
     inputs = dict(u=u, delta=delta, A=A, B=B, C=C, D=D, z=z, delta_bias=delta_bias)
+    if pq_rank:
+        # magnitudes like a trained motif adapter: P, Q ~ N(0, 0.5) (the module scales P by pq_k)
+        if pq_per_dim:
+            inputs["P"] = 0.5 * torch.randn(dim, dstate, pq_rank, generator=g)
+            inputs["Q"] = 0.5 * torch.randn(dim, pq_rank, dstate, generator=g)
+        else:
+            inputs["P"] = 0.5 * torch.randn(dstate, pq_rank, generator=g)
+            inputs["Q"] = 0.5 * torch.randn(pq_rank, dstate, generator=g)
     leaves = {k: (v.clone().requires_grad_(grads) if v is not None else None) for k, v in inputs.items()}
     out, last_state = ssi.selective_scan_ref(
         leaves["u"], leaves["delta"], leaves["A"], leaves["B"], leaves["C"], leaves["D"],
-        z=leaves["z"], delta_bias=leaves["delta_bias"], delta_softplus=softplus, return_last_state=True)
+        z=leaves["z"], delta_bias=leaves["delta_bias"], delta_softplus=softplus, return_last_state=True,
+        P=leaves.get("P"), Q=leaves.get("Q"))
     rec = dict(name=name, kind="scan", softplus=softplus, inputs=inputs, dout=dout,
                out=out.detach(), last_state=last_state.detach())
     if grads:
@@ -203,6 +213,9 @@ def main():
     scan_case(ssi, "n4_L1", batch=2, dim=4, seqlen=1, dstate=4, seed=4)
     scan_case(ssi, "long2100", batch=1, dim=2, seqlen=2100, dstate=16, seed=5)
     scan_case(ssi, "noD_n32", batch=1, dim=4, seqlen=70, dstate=32, has_D=False, seed=6)
+    scan_case(ssi, "pq2_shared", batch=2, dim=16, seqlen=300, dstate=16, pq_rank=2, seed=7)
+    scan_case(ssi, "pq4_perdim_noz", batch=1, dim=8, seqlen=70, dstate=8, pq_rank=4, pq_per_dim=True,
+              has_z=False, seed=8)
     inner_case(ssi, "small")
     module_case(msm, "small")
 

@@ -9,7 +9,8 @@ import torch
 
 
 def make_scan_inputs(batch, dim, seqlen, dstate, dtype=torch.float32, groups=0, has_z=True, has_D=True,
-                     has_bias=True, softplus=True, seed=0, device="cpu", random_A=False):
+                     has_bias=True, softplus=True, seed=0, device="cpu", random_A=False, pq_rank=0,
+                     pq_per_dim=False, pq_scale=0.5):
     g = torch.Generator().manual_seed(seed)
     u = torch.randn(batch, dim, seqlen, generator=g)
     if softplus:
@@ -28,10 +29,20 @@ def make_scan_inputs(batch, dim, seqlen, dstate, dtype=torch.float32, groups=0, 
     z = torch.randn(batch, dim, seqlen, generator=g) if has_z else None
     bias = torch.log(torch.expm1(torch.rand(dim, generator=g) * (0.1 - 1e-3) + 1e-3)) if has_bias else None
     dout = torch.randn(batch, dim, seqlen, generator=g)
+    P = Q = None
+    if pq_rank:  # motif coupling, fp32 (drawn after everything else: other tensors unchanged)
+        if pq_per_dim:
+            P = pq_scale * torch.randn(dim, dstate, pq_rank, generator=g)
+            Q = pq_scale * torch.randn(dim, pq_rank, dstate, generator=g)
+        else:
+            P = pq_scale * torch.randn(dstate, pq_rank, generator=g)
+            Q = pq_scale * torch.randn(pq_rank, dstate, generator=g)
     cast = lambda t: None if t is None else t.to(dtype).to(device)
     keep = lambda t: None if t is None else t.float().to(device)
     inputs = dict(u=cast(u), delta=cast(delta), A=keep(A), B=cast(B), C=cast(C), D=keep(D), z=cast(z),
                   delta_bias=keep(bias))
+    if pq_rank:
+        inputs["P"], inputs["Q"] = keep(P), keep(Q)
     return inputs, cast(dout)
 
 

@@ -116,5 +116,9 @@ def test_python_shim_raises_on_unbuilt_paths():
     u = torch.zeros(1, 2, 4)
     A = -torch.ones(2, 4)
     B = torch.zeros(1, 4, 4)
-    with pytest.raises(NotImplementedError):
-        selective_scan_fn(u, u, A, B, B, P=torch.zeros(4, 2), Q=torch.zeros(2, 4))
+    with pytest.raises(NotImplementedError):      # complex A
+        selective_scan_fn(u, u, torch.complex(A, A), B, B)
+    with pytest.raises(NotImplementedError):      # complex A on the P/Q path
+        selective_scan_fn(u, u, torch.complex(A, A), B, B, P=torch.zeros(4, 2), Q=torch.zeros(2, 4))
+    with pytest.raises(ValueError):               # P without Q
+        selective_scan_fn(u, u, A, B, B, P=torch.zeros(4, 2))

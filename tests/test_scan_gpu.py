@@ -25,7 +25,8 @@ def run_kernel(inputs, dout, softplus, backward=True):
               for k, v in inputs.items()}
     out, last = selective_scan_fn(leaves["u"], leaves["delta"], leaves["A"], leaves["B"], leaves["C"],
                                   leaves["D"], z=leaves["z"], delta_bias=leaves["delta_bias"],
-                                  delta_softplus=softplus, return_last_state=True)
+                                  delta_softplus=softplus, return_last_state=True,
+                                  P=leaves.get("P"), Q=leaves.get("Q"))
     grads = None
     if backward:
         out.backward(dout.to(DEV))
@@ -40,7 +41,7 @@ def compare(out, last, grads, ref_out, ref_last, ref_grads, dtype, what=""):
     assert_close(out, ref_out, t, t, f"{what} out")
     assert_close(last, ref_last, t, t, f"{what} last_state")
     if grads is not None:
-        for k in GRAD_KEYS:
+        for k in GRAD_KEYS + tuple(k for k in ("P", "Q") if ref_grads.get(k) is not None):
             if ref_grads.get(k) is None:
                 assert grads[k] is None, k
                 continue
