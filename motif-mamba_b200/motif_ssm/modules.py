@@ -1,7 +1,8 @@
 """MotifMamba mixer and LM stack on this library's kernels (callers of the hot path).
 
-* ``Mambamotif`` -- the reference mixer (``mamba_ssm/modules/mamba_simplemotif.py:31-443``)
-  for ``pq_rank = 0`` (the motif P/Q path is not built and raises).  Parameter names,
+* ``Mambamotif`` -- the reference mixer (``mamba_ssm/modules/mamba_simplemotif.py:31-443``),
+  including the motif low-rank coupling (``pq_rank > 0``: fp32 ``P``, ``Q`` and the scalar
+  ``pq_k``, scan with ``P_eff = pq_k * P``; ``:138-155, 270-335``).  Parameter names,
   shapes and initialisation follow the reference (dt-bias inverse-softplus init ``:102-110``,
   S4D-real ``A_log`` ``:116-123``, ``D = 1`` ``:135``).  Prefill runs ``mamba_inner_fn``
   (fused conv -> x_proj -> dt_proj -> scan -> out_proj); with an inference cache it runs
@@ -36,10 +37,9 @@ class Mambamotif(nn.Module):
                  dt_init="random", dt_scale=1.0, dt_init_floor=1e-4, conv_bias=True, bias=False,
                  use_fast_path=True, layer_idx=None, pq_rank=0, pq_per_dim=False, pq_k_init=1e-4,
                  device=None, dtype=None):
-        if pq_rank:
-            raise NotImplementedError("Mambamotif: the P/Q (motif low-rank) path is not built in this library")
         fk = {"device": device, "dtype": dtype}
         super().__init__()
+        self.pq_rank, self.pq_per_dim = int(pq_rank), bool(pq_per_dim)
         self.d_model, self.d_state, self.d_conv, self.expand = d_model, d_state, d_conv, expand
         self.d_inner = int(expand * d_model)
         self.dt_rank = math.ceil(d_model / 16) if dt_rank == "auto" else dt_rank
@@ -68,10 +68,85 @@ class Mambamotif(nn.Module):
         self.A_log._no_weight_decay = True
         self.D = nn.Parameter(torch.ones(self.d_inner, device=device))
         self.D._no_weight_decay = True
-        self.register_parameter("P", None)
-        self.register_parameter("Q", None)
-        self.register_parameter("pq_k", None)
+        if self.pq_rank > 0:  # N(0, 1e-2) factors, fp32 whatever the module dtype (:140-151)
+            if self.pq_per_dim:
+                P = torch.empty(self.d_inner, d_state, self.pq_rank, device=device)
+                Q = torch.empty(self.d_inner, self.pq_rank, d_state, device=device)
+            else:
+                P = torch.empty(d_state, self.pq_rank, device=device)
+                Q = torch.empty(self.pq_rank, d_state, device=device)
+            nn.init.normal_(P, std=1e-2)
+            nn.init.normal_(Q, std=1e-2)
+            self.P = nn.Parameter(P)
+            self.Q = nn.Parameter(Q)
+            self.pq_k = nn.Parameter(torch.tensor(float(pq_k_init), device=device, dtype=torch.float32))
+        else:
+            self.register_parameter("P", None)
+            self.register_parameter("Q", None)
+            self.register_parameter("pq_k", None)
         self.out_proj = nn.Linear(self.d_inner, d_model, bias=bias, **fk)
+
+    @staticmethod
+    def _extract_state_dict(raw_obj, state_dict_key=None):
+        """The state dict inside a checkpoint object (mamba_simplemotif.py:159-170)."""
+        if not isinstance(raw_obj, dict):
+            raise ValueError("Checkpoint must be a dict or contain a dict-like state_dict")
+        if state_dict_key is not None:
+            if not isinstance(raw_obj.get(state_dict_key), dict):
+                raise ValueError(f"state_dict_key='{state_dict_key}' not found in checkpoint")
+            return raw_obj[state_dict_key]
+        for k in ("state_dict", "model_state_dict", "model", "net"):
+            if isinstance(raw_obj.get(k), dict):
+                return raw_obj[k]
+        return raw_obj
+
+    def load_checkpoint(self, checkpoint_path, strict=False, state_dict_key=None, strip_module_prefix=True):
+        """Load weights; returns the missing / unexpected keys (mamba_simplemotif.py:172-189)."""
+        state = self._extract_state_dict(torch.load(checkpoint_path, map_location="cpu"), state_dict_key)
+        cleaned = {}
+        for k, v in state.items():
+            if isinstance(v, torch.Tensor):
+                if strip_module_prefix and k.startswith("module."):
+                    k = k[len("module."):]
+                cleaned[k] = v
+        res = self.load_state_dict(cleaned, strict=strict)
+        return {"missing_keys": list(res.missing_keys), "unexpected_keys": list(res.unexpected_keys)}
+
+    @classmethod
+    def create(cls, *, init_mode="scratch", checkpoint_path=None, model_size=None, load_strict=False,
+               train_pq_only=False, state_dict_key=None, **kwargs):
+        """Scratch or checkpoint construction (mamba_simplemotif.py:191-228); returns
+        ``(model, load_info)``."""
+        if model_size is not None:
+            if model_size not in cls.SIZE_PRESETS:
+                raise ValueError(f"Unknown model_size='{model_size}', choose from {list(cls.SIZE_PRESETS)}")
+            cfg = dict(cls.SIZE_PRESETS[model_size])
+            cfg.update(kwargs)
+        else:
+            cfg = dict(kwargs)
+        model = cls(**cfg)
+        info = {"missing_keys": [], "unexpected_keys": []}
+        if init_mode == "load":
+            if checkpoint_path is None:
+                raise ValueError("checkpoint_path is required when init_mode='load'")
+            info = model.load_checkpoint(checkpoint_path, strict=load_strict, state_dict_key=state_dict_key)
+        elif init_mode != "scratch":
+            raise ValueError("init_mode must be 'scratch' or 'load'")
+        if train_pq_only:
+            model.set_train_pq_only(True)
+        return model, info
+
+    def set_train_pq_only(self, enable=True):
+        """Freeze everything but P, Q and pq_k (mamba_simplemotif.py:230-239)."""
+        if self.P is None or self.Q is None:
+            raise RuntimeError("P/Q are not initialized. Set pq_rank > 0 when constructing Mambamotif.")
+        for p in self.parameters():
+            p.requires_grad_(not enable)
+        for p in (self.P, self.Q, self.pq_k):
+            p.requires_grad_(True)
+
+    def _P_eff(self):
+        return None if self.P is None else self.pq_k * self.P
 
     def forward(self, hidden_states, inference_params=None):
         """hidden_states (B, L, D) -> (B, L, D)."""
@@ -88,7 +163,7 @@ class Mambamotif(nn.Module):
         if self.in_proj.bias is not None:
             xz = xz + self.in_proj.bias.to(xz.dtype).unsqueeze(-1)
         A = -torch.exp(self.A_log.float())
-        if self.use_fast_path and inference_params is None:
+        if self.use_fast_path and self.P is None and inference_params is None:
             return mamba_inner_fn(xz, self.conv1d.weight, self.conv1d.bias, self.x_proj.weight,
                                   self.dt_proj.weight, self.out_proj.weight, self.out_proj.bias, A, None, None,
                                   self.D.float(), delta_bias=self.dt_proj.bias.float(), delta_softplus=True)
@@ -103,14 +178,20 @@ class Mambamotif(nn.Module):
         B = B.view(batch, seqlen, -1).transpose(1, 2).contiguous()
         C = C.view(batch, seqlen, -1).transpose(1, 2).contiguous()
         y = selective_scan_fn(x, dt, A, B, C, self.D.float(), z=z, delta_bias=self.dt_proj.bias.float(),
-                              delta_softplus=True, return_last_state=ssm_state is not None)
+                              delta_softplus=True, return_last_state=ssm_state is not None,
+                              P=self._P_eff(), Q=self.Q)
         if ssm_state is not None:
             y, last_state = y
             ssm_state.copy_(last_state)
         return self.out_proj(y.transpose(1, 2))
 
     def step(self, hidden_states, conv_state, ssm_state):
-        """One decode token (mamba_simplemotif.py:337-402); states are updated in place."""
+        """One decode token (mamba_simplemotif.py:337-402); states are updated in place.
+
+        With P / Q the reference runs a one-step ``selective_scan_fn`` (``:367-395``), which
+        starts from a zero state rather than from ``ssm_state`` and then overwrites
+        ``ssm_state`` with that step's state; this restatement keeps that behaviour so that
+        decode outputs match the reference's."""
         assert hidden_states.shape[1] == 1, "decoding one token at a time"
         xz = self.in_proj(hidden_states.squeeze(1))
         x, z = xz.chunk(2, dim=-1)
@@ -120,6 +201,14 @@ class Mambamotif(nn.Module):
         dt, B, C = torch.split(x_db, [self.dt_rank, self.d_state, self.d_state], dim=-1)
         dt = F.linear(dt, self.dt_proj.weight)
         A = -torch.exp(self.A_log.float())
+        if self.P is not None:
+            dt = F.softplus(dt + self.dt_proj.bias.to(dtype=dt.dtype))
+            y, last_state = selective_scan_fn(x.unsqueeze(-1), dt.unsqueeze(-1), A, B.unsqueeze(-1),
+                                              C.unsqueeze(-1), D=self.D.float(), z=z.unsqueeze(-1),
+                                              delta_bias=None, delta_softplus=False, return_last_state=True,
+                                              P=self._P_eff(), Q=self.Q)
+            ssm_state.copy_(last_state.to(ssm_state.dtype))
+            return self.out_proj(y[..., 0]).unsqueeze(1), conv_state, ssm_state
         y = selective_state_update(ssm_state, x, dt, A, B, C, self.D, z=z, dt_bias=self.dt_proj.bias,
                                    dt_softplus=True)
         return self.out_proj(y).unsqueeze(1), conv_state, ssm_state
@@ -306,6 +395,8 @@ class TPMambamotif(nn.Module):
 
     @classmethod
     def from_full(cls, full, rank, world, group):
+        if full.P is not None:
+            raise NotImplementedError("tensor-parallel sharding of the P/Q coupling is not implemented")
         di = full.d_inner
         assert di % world == 0, "d_inner must divide by the tensor-parallel size"
         dl = di // world

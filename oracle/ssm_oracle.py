@@ -19,6 +19,9 @@ reference's own pure-torch path (4354ce38/Motif-Mamba, a fork of mamba_ssm
 * ``causal_conv1d_update_ref``  <- ``mamba_ssm/modules/mamba_simplemotif.py:344-350``
 * ``selective_state_update_ref``<- ``mamba_ssm/modules/mamba_simplemotif.py:367-376``
                                    (fallback for the missing Triton kernel)
+* ``mixer_pq_prefill_ref``      <- ``mamba_ssm/modules/mamba_simplemotif.py:256-335`` (slow
+                                   path with ``P_eff = pq_k * P``)
+* ``mixer_pq_step_ref``         <- ``mamba_ssm/modules/mamba_simplemotif.py:337-402`` (P/Q step)
 * ``rms_norm_ref``              <- x * rsqrt(mean(x^2) + eps) * w, the RMSNorm the
                                    stack uses (``mamba_ssm/models/mixer_seq_simple.py:64-66``,
                                    eps default ``:35``); the Triton source is missing.
@@ -186,6 +189,46 @@ def mamba_inner_ref(xz, conv1d_weight, conv1d_bias, x_proj_weight, delta_proj_we
     y = selective_scan_ref(x, delta, A, B, C, D, z=z, delta_bias=delta_bias,
                            delta_softplus=delta_softplus)
     return F.linear(y.transpose(1, 2), out_proj_weight, out_proj_bias)
+
+
+def mixer_pq_prefill_ref(sd, hidden, return_last_state=False):
+    """Mambamotif slow-path prefill with the P/Q coupling (mamba_simplemotif.py:256-335):
+    in_proj -> causal conv + SiLU -> x_proj -> dt_proj -> scan with ``P_eff = pq_k * P`` ->
+    out_proj.  ``sd`` is the module's state dict (fp32)."""
+    batch, seqlen, _ = hidden.shape
+    xz = torch.einsum("od,bld->bol", sd["in_proj.weight"], hidden)
+    x, z = xz.chunk(2, dim=1)
+    x = causal_conv1d_ref(x, sd["conv1d.weight"][:, 0, :], sd["conv1d.bias"], "silu")
+    n = sd["A_log"].shape[1]
+    dt_rank = sd["dt_proj.weight"].shape[1]
+    x_dbl = torch.einsum("bdl,od->blo", x, sd["x_proj.weight"])
+    dt, B, C = torch.split(x_dbl, [dt_rank, n, n], dim=-1)
+    dt = torch.einsum("blr,dr->bdl", dt, sd["dt_proj.weight"])
+    A = -torch.exp(sd["A_log"].float())
+    y = selective_scan_ref(x, dt, A, B.transpose(1, 2), C.transpose(1, 2), sd["D"].float(), z=z,
+                           delta_bias=sd["dt_proj.bias"].float(), delta_softplus=True,
+                           return_last_state=return_last_state, P=sd["pq_k"] * sd["P"], Q=sd["Q"])
+    y, last = y if return_last_state else (y, None)
+    out = torch.einsum("bdl,od->blo", y, sd["out_proj.weight"])
+    return (out, last) if return_last_state else out
+
+
+def mixer_pq_step_ref(sd, hidden, conv_state, ssm_state):
+    """Mambamotif.step with the P/Q coupling (mamba_simplemotif.py:337-395): conv update, then
+    a one-step scan that starts from a zero state (the reference does not feed ``ssm_state``
+    in), whose final state overwrites ``ssm_state``.  Updates the states in place."""
+    xz = hidden[:, 0] @ sd["in_proj.weight"].t()
+    x, z = xz.chunk(2, dim=-1)
+    x = causal_conv1d_update_ref(x, conv_state, sd["conv1d.weight"][:, 0, :], sd["conv1d.bias"], "silu")
+    n = sd["A_log"].shape[1]
+    dt_rank = sd["dt_proj.weight"].shape[1]
+    dt, B, C = torch.split(x @ sd["x_proj.weight"].t(), [dt_rank, n, n], dim=-1)
+    dt = _softplus(dt @ sd["dt_proj.weight"].t() + sd["dt_proj.bias"])
+    A = -torch.exp(sd["A_log"].float())
+    y, last = selective_scan_ref(x[..., None], dt[..., None], A, B[..., None], C[..., None], sd["D"].float(),
+                                 z=z[..., None], return_last_state=True, P=sd["pq_k"] * sd["P"], Q=sd["Q"])
+    ssm_state.copy_(last)
+    return (y[..., 0] @ sd["out_proj.weight"].t())[:, None]
 
 
 def rms_norm_ref(x, weight, eps=1e-5):

@@ -159,12 +159,22 @@ def inner_case(ssi, name, *, batch=2, d_model=16, expand=2, dstate=8, dt_rank=4,
     print("wrote inner", name, tuple(out.shape))
 
 
-def module_case(msm, name, *, batch=2, d_model=16, d_state=8, prefill=12, steps=3, seed=0):
-    """Mambamotif prefill (slow path) + decode steps through the module's torch fallbacks."""
+def module_case(msm, name, *, batch=2, d_model=16, d_state=8, prefill=12, steps=3, seed=0, pq_rank=0,
+                pq_per_dim=False, pq_k=8.0):
+    """Mambamotif prefill (slow path) + decode steps through the module's torch fallbacks.
+    With ``pq_rank`` the P / Q factors and ``pq_k`` are redrawn large enough (N(0, 0.5) and ``pq_k``)
+    that the coupling visibly changes the outputs."""
     torch.manual_seed(seed)
     mod = msm.Mambamotif(d_model=d_model, d_state=d_state, d_conv=4, expand=2,
-                         use_fast_path=False, layer_idx=0)
+                         use_fast_path=False, layer_idx=0, pq_rank=pq_rank, pq_per_dim=pq_per_dim)
     g = torch.Generator().manual_seed(seed + 1)
+    pq = {}
+    if pq_rank:
+        with torch.no_grad():
+            mod.P.copy_(0.5 * torch.randn(mod.P.shape, generator=g))
+            mod.Q.copy_(0.5 * torch.randn(mod.Q.shape, generator=g))
+            mod.pq_k.fill_(pq_k)
+        pq = dict(P=mod.pq_k * mod.P, Q=mod.Q)
     hs = torch.randn(batch, prefill, d_model, generator=g)
     with torch.no_grad():
         y_prefill = mod(hs)
@@ -183,7 +193,7 @@ def module_case(msm, name, *, batch=2, d_model=16, d_state=8, prefill=12, steps=
         A = -torch.exp(mod.A_log.float())
         _, last = msm.selective_scan_fn(x_act, dt, A, Bm, Cm, mod.D.float(), z=z,
                                         delta_bias=mod.dt_proj.bias.float(), delta_softplus=True,
-                                        return_last_state=True)
+                                        return_last_state=True, **pq)
         ssm_state.copy_(last)
         conv0, ssm0 = conv_state.clone(), ssm_state.clone()
         step_in, step_out = [], []
@@ -192,7 +202,8 @@ def module_case(msm, name, *, batch=2, d_model=16, d_state=8, prefill=12, steps=
             o, _, _ = mod.step(h1, conv_state, ssm_state)
             step_in.append(h1)
             step_out.append(o)
-    rec = dict(name=name, kind="module", config=dict(d_model=d_model, d_state=d_state, d_conv=4, expand=2),
+    rec = dict(name=name, kind="module", config=dict(d_model=d_model, d_state=d_state, d_conv=4, expand=2,
+                                                     pq_rank=pq_rank, pq_per_dim=pq_per_dim),
                state_dict={k: v.clone() for k, v in mod.state_dict().items()},
                hidden=hs, y_prefill=y_prefill, conv_state0=conv0, ssm_state0=ssm0,
                step_in=torch.stack(step_in), step_out=torch.stack(step_out),
@@ -218,6 +229,8 @@ def main():
               has_z=False, seed=8)
     inner_case(ssi, "small")
     module_case(msm, "small")
+    module_case(msm, "pq2", pq_rank=2, seed=3, pq_k=40.0)
+    module_case(msm, "pq3_perdim", d_state=16, pq_rank=3, pq_per_dim=True, seed=4)
 
 
 if __name__ == "__main__":

@@ -13,12 +13,13 @@ GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 DEV = "cuda"
 
 
-def _golden_module():
+def _golden_module(name="small"):
     from motif_ssm.modules import Mambamotif
-    rec = torch.load(os.path.join(GOLD, "module_small.pt"), weights_only=False)
+    rec = torch.load(os.path.join(GOLD, f"module_{name}.pt"), weights_only=False)
     cfg = rec["config"]
     mod = Mambamotif(d_model=cfg["d_model"], d_state=cfg["d_state"], d_conv=cfg["d_conv"], expand=cfg["expand"],
-                     layer_idx=0, device=DEV)
+                     layer_idx=0, pq_rank=cfg.get("pq_rank", 0), pq_per_dim=cfg.get("pq_per_dim", False),
+                     device=DEV)
     mod.load_state_dict({k: v.to(DEV) for k, v in rec["state_dict"].items()})
     return rec, mod
 
@@ -30,9 +31,19 @@ def test_mixer_prefill_matches_reference_module():
     assert_close(y, rec["y_prefill"], 1e-3, 1e-3, "Mambamotif prefill")
 
 
-def test_mixer_prefill_with_cache_then_decode_matches_reference_module():
+@pytest.mark.parametrize("name", ["pq2", "pq3_perdim"])
+def test_pq_mixer_prefill_matches_reference_module(name):
+    """Mambamotif with the motif P/Q coupling (pq_k * P, Q) on the ss_pq kernels."""
+    rec, mod = _golden_module(name)
+    with torch.no_grad():
+        y = mod(rec["hidden"].to(DEV))
+    assert_close(y, rec["y_prefill"], 1e-3, 1e-3, f"{name} prefill")
+
+
+@pytest.mark.parametrize("name", ["small", "pq2", "pq3_perdim"])
+def test_mixer_prefill_with_cache_then_decode_matches_reference_module(name):
     from motif_ssm.modules import InferenceParams
-    rec, mod = _golden_module()
+    rec, mod = _golden_module(name)
     hs = rec["hidden"].to(DEV)
     params = InferenceParams(max_seqlen=64, max_batch_size=hs.shape[0])
     with torch.no_grad():
@@ -130,3 +141,27 @@ def test_graphed_decode_matches_eager_decode():
             pe.seqlen_offset += 1
             graphed = dec.step(ids[:, t:t + 1])
             assert torch.equal(graphed, eager), t
+
+
+def test_pq_mixer_trains_pq_only():
+    """``create(train_pq_only=True)`` leaves only P, Q, pq_k trainable; their gradients
+    through the module match autograd through the CPU oracle's slow-path restatement."""
+    from motif_ssm.modules import Mambamotif
+    torch.manual_seed(4)
+    mod, info = Mambamotif.create(d_model=32, d_state=16, pq_rank=2, train_pq_only=True, layer_idx=0, device=DEV)
+    assert info == {"missing_keys": [], "unexpected_keys": []}
+    assert sorted(n for n, p in mod.named_parameters() if p.requires_grad) == ["P", "Q", "pq_k"]
+    with torch.no_grad():
+        mod.pq_k.fill_(20.0)
+        mod.P.normal_(0, 0.5)
+        mod.Q.normal_(0, 0.5)
+    g = torch.Generator().manual_seed(5)
+    hs = torch.randn(2, 100, 32, generator=g)
+    w = torch.randn(2, 100, 32, generator=g)
+    (mod(hs.to(DEV)) * w.to(DEV)).sum().backward()
+    sd = {k: v.detach().float().cpu().clone() for k, v in mod.state_dict().items()}
+    for k in ("P", "Q", "pq_k"):
+        sd[k].requires_grad_(True)
+    (O.mixer_pq_prefill_ref(sd, hs) * w).sum().backward()
+    for k in ("P", "Q", "pq_k"):
+        assert_close(getattr(mod, k).grad, sd[k].grad, 1e-3, 1e-3, f"d{k}")

@@ -86,3 +86,20 @@ def test_module_prefill_oracle_matches_reference():
                             sd["dt_proj.weight"], sd["out_proj.weight"], None, A, None, None,
                             sd["D"].float(), delta_bias=sd["dt_proj.bias"].float())
     torch.testing.assert_close(out, rec["y_prefill"], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("name", ["pq2", "pq3_perdim"])
+def test_module_pq_oracle_matches_reference(name):
+    """Mambamotif with the P/Q coupling: slow-path prefill, cache states and decode steps."""
+    rec = _load(os.path.join(GOLD, f"module_{name}.pt"))
+    sd = rec["state_dict"]
+    out, last = O.mixer_pq_prefill_ref(sd, rec["hidden"], return_last_state=True)
+    torch.testing.assert_close(out, rec["y_prefill"], rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(last, rec["ssm_state0"], rtol=1e-5, atol=1e-5)
+    conv_state = rec["conv_state0"].clone()
+    ssm_state = rec["ssm_state0"].clone()
+    for i in range(rec["step_in"].shape[0]):
+        o = O.mixer_pq_step_ref(sd, rec["step_in"][i], conv_state, ssm_state)
+        torch.testing.assert_close(o, rec["step_out"][i], rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(conv_state, rec["conv_state_final"])
+    torch.testing.assert_close(ssm_state, rec["ssm_state_final"], rtol=1e-5, atol=1e-5)
