@@ -28,6 +28,8 @@ def make_scan_inputs(batch, dim, seqlen, dstate, dtype=torch.float32, groups=0, 
     D = (1.0 + 0.1 * torch.randn(dim, generator=g)) if has_D else None
     z = torch.randn(batch, dim, seqlen, generator=g) if has_z else None
     bias = torch.log(torch.expm1(torch.rand(dim, generator=g) * (0.1 - 1e-3) + 1e-3)) if has_bias else None
+    if has_bias and not softplus:  # dt = delta + bias must stay positive without softplus
+        bias = -0.05 * bias
     dout = torch.randn(batch, dim, seqlen, generator=g)
     P = Q = None
     if pq_rank:  # motif coupling, fp32 (drawn after everything else: other tensors unchanged)
@@ -61,11 +63,12 @@ def assert_close(actual, expected, rtol, atol, name=""):
     e = expected.detach().float().cpu()
     assert a.shape == e.shape, f"{name}: shape {tuple(a.shape)} != {tuple(e.shape)}"
     scale = max(1.0, e.abs().max().item()) if e.numel() else 1.0
+    assert torch.isfinite(e).all(), f"{name}: expected values are not finite"
     err = (a - e).abs()
     bound = atol * scale + rtol * e.abs()
-    bad = err > bound
+    bad = ~(err <= bound)  # NaN / inf in the actual values count as mismatches
     if bad.any():
-        i = int(torch.argmax((err - bound).flatten()))
+        i = int(torch.argmax(torch.nan_to_num(err - bound, nan=float("inf")).flatten()))
         raise AssertionError(
             f"{name}: {int(bad.sum())}/{e.numel()} elements out of tolerance; worst at flat index {i}: "
             f"actual {a.flatten()[i].item():.6g} expected {e.flatten()[i].item():.6g} "
