@@ -145,12 +145,24 @@ def selective_scan_fn(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_
     return SelectiveScanFn.apply(u, delta, A, B, C, D, z, delta_bias, delta_softplus, return_last_state)
 
 
+def _rms_along(t, weight, eps, dim):
+    """RMSNorm of ``t`` along ``dim`` (fp32 math, output in t's dtype, contiguous):
+    t * rsqrt(mean(t^2) + eps) * weight -- the reference's ``rms_norm_forward`` over the rows
+    it rearranges to (``selective_scan_interface.py:217-234, 521-532``)."""
+    tf = t.float()
+    shape = [1] * t.dim()
+    shape[dim] = -1
+    y = tf * torch.rsqrt(tf.pow(2).mean(dim=dim, keepdim=True) + eps) * weight.float().view(shape)
+    return y.to(t.dtype).contiguous()
+
+
 class MambaInnerFn(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, xz, conv1d_weight, conv1d_bias, x_proj_weight, delta_proj_weight, out_proj_weight,
                 out_proj_bias, A, B=None, C=None, D=None, delta_bias=None, B_proj_bias=None,
-                C_proj_bias=None, delta_softplus=True, checkpoint_lvl=1):
+                C_proj_bias=None, delta_softplus=True, checkpoint_lvl=1, b_rms_weight=None, c_rms_weight=None,
+                dt_rms_weight=None, b_c_dt_rms_eps=1e-6):
         assert checkpoint_lvl in (0, 1)
         if A.is_complex():
             raise NotImplementedError("mamba_inner_fn: complex A is not supported by this library")
@@ -192,6 +204,15 @@ class MambaInnerFn(torch.autograd.Function):
             C = _last_dim_contig(C)
         if D is not None:
             D = D.contiguous()
+        # optional RMSNorm of B / C over dstate and of delta over channels, applied to the scan
+        # inputs as the reference does (selective_scan_interface.py:521-532)
+        if b_rms_weight is not None:
+            B = _rms_along(B, b_rms_weight, b_c_dt_rms_eps, dim=2)
+        if c_rms_weight is not None:
+            C = _rms_along(C, c_rms_weight, b_c_dt_rms_eps, dim=2)
+        if dt_rms_weight is not None:
+            delta = _rms_along(delta, dt_rms_weight, b_c_dt_rms_eps, dim=1)
+        ctx.rms = (b_rms_weight, c_rms_weight, dt_rms_weight, b_c_dt_rms_eps)
         out, scan_x, out_z = selective_scan_cuda.fwd(conv_out, delta, A, B, C, D=D, z=z, delta_bias=delta_bias,
                                                      delta_softplus=delta_softplus)
         ctx.delta_softplus = delta_softplus
@@ -216,6 +237,16 @@ class MambaInnerFn(torch.autograd.Function):
         if ctx.checkpoint_lvl == 1:
             conv_out = causal_conv1d_fwd_function(x, w_conv, conv1d_bias, None, None, None, True)
             delta = (delta_proj_weight @ x_dbl[:, :rank].t()).view(-1, batch, L).transpose(0, 1)
+            # the reference's recompute (selective_scan_interface.py:572-589): delta is normalised
+            # again from the projection, and the SAVED (already normalised) B / C are normalised
+            # a second time; both are kept so that the gradients equal the reference's
+            b_rms, c_rms, dt_rms, eps = ctx.rms
+            if dt_rms is not None:
+                delta = _rms_along(delta, dt_rms, eps, dim=1)
+            if b_rms is not None:
+                B = _rms_along(B, b_rms, eps, dim=2)
+            if c_rms is not None:
+                C = _rms_along(C, c_rms, eps, dim=2)
         dxz = torch.empty_like(xz)
         dx, dz = dxz.chunk(2, dim=1)
         dout2 = dout.reshape(-1, dout.shape[-1]).t()              # (e, b*l)
@@ -252,15 +283,18 @@ class MambaInnerFn(torch.autograd.Function):
         dconv_w = dconv_w.unsqueeze(1)
         return (dxz, dconv_w, dconv_b, dx_proj_weight, ddelta_proj_weight, dout_proj_weight, dout_proj_bias,
                 dA, dB, dC, dD, ddelta_bias if delta_bias is not None else None, dB_proj_bias, dC_proj_bias,
-                None, None)
+                None, None, None, None, None, None)
 
 
 def mamba_inner_fn(xz, conv1d_weight, conv1d_bias, x_proj_weight, delta_proj_weight, out_proj_weight,
                    out_proj_bias, A, B=None, C=None, D=None, delta_bias=None, B_proj_bias=None,
                    C_proj_bias=None, delta_softplus=True, checkpoint_lvl=1, b_rms_weight=None,
                    c_rms_weight=None, dt_rms_weight=None, b_c_dt_rms_eps=1e-6):
-    if b_rms_weight is not None or c_rms_weight is not None or dt_rms_weight is not None:
-        raise NotImplementedError("mamba_inner_fn: the B/C/dt RMSNorm options are not built in this library")
+    """With ``b_rms_weight`` / ``c_rms_weight`` / ``dt_rms_weight`` the scan's B, C (over
+    dstate) and delta (over channels) are RMS-normalised first.  As in the reference's
+    backward (``selective_scan_interface.py:597-645``), the gradients of B, C and delta pass
+    to x_proj / dt_proj as if the normalisation were the identity, and the norm weights get
+    no gradient."""
     return MambaInnerFn.apply(xz, conv1d_weight, conv1d_bias, x_proj_weight, delta_proj_weight, out_proj_weight,
                               out_proj_bias, A, B, C, D, delta_bias, B_proj_bias, C_proj_bias, delta_softplus,
-                              checkpoint_lvl)
+                              checkpoint_lvl, b_rms_weight, c_rms_weight, dt_rms_weight, b_c_dt_rms_eps)

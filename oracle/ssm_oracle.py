@@ -162,11 +162,29 @@ def selective_state_update_ref(state, x, dt, A, B, C, D=None, z=None, dt_bias=No
     return y.to(dtype)
 
 
+def _rms_straight_through(t, weight, eps, dim):
+    """RMSNorm of t along ``dim`` (fp32 math, t's dtype) whose gradient is passed through
+    unchanged, as the reference's ``MambaInnerFn.backward`` treats it."""
+    tf = t.detach().float()
+    shape = [1] * t.dim()
+    shape[dim] = -1
+    y = (tf * torch.rsqrt(tf.pow(2).mean(dim=dim, keepdim=True) + eps) * weight.detach().float().view(shape))
+    y = y.to(t.dtype)
+    return t + (y - t).detach()
+
+
 def mamba_inner_ref(xz, conv1d_weight, conv1d_bias, x_proj_weight, delta_proj_weight,
                     out_proj_weight, out_proj_bias, A, B=None, C=None, D=None, delta_bias=None,
-                    B_proj_bias=None, C_proj_bias=None, delta_softplus=True):
+                    B_proj_bias=None, C_proj_bias=None, delta_softplus=True, b_rms_weight=None,
+                    c_rms_weight=None, dt_rms_weight=None, b_c_dt_rms_eps=1e-6):
     """Mamba-1 inner block (selective_scan_interface.py:659-694): conv+SiLU -> x_proj ->
-    dt_proj -> selective scan (z-gated, softplus) -> out_proj."""
+    dt_proj -> selective scan (z-gated, softplus) -> out_proj.
+
+    The optional RMSNorm weights follow ``MambaInnerFn`` (``:521-532``): B and C are
+    normalised over dstate and delta over channels before the scan.  Their backward is the
+    identity (the reference's backward, ``:597-645``, passes the scan's dB / dC / ddelta
+    straight to x_proj and dt_proj), so autograd through this function reproduces those
+    gradients."""
     L = xz.shape[-1]
     delta_rank = delta_proj_weight.shape[1]
     d_state = A.shape[-1]
@@ -186,6 +204,12 @@ def mamba_inner_ref(xz, conv1d_weight, conv1d_bias, x_proj_weight, delta_proj_we
         if C_proj_bias is not None:
             C = C + C_proj_bias.to(C.dtype)
         C = C.reshape(-1, L, d_state).transpose(1, 2).contiguous()
+    if b_rms_weight is not None:
+        B = _rms_straight_through(B, b_rms_weight, b_c_dt_rms_eps, -2)
+    if c_rms_weight is not None:
+        C = _rms_straight_through(C, c_rms_weight, b_c_dt_rms_eps, -2)
+    if dt_rms_weight is not None:
+        delta = _rms_straight_through(delta, dt_rms_weight, b_c_dt_rms_eps, 1)
     y = selective_scan_ref(x, delta, A, B, C, D, z=z, delta_bias=delta_bias,
                            delta_softplus=delta_softplus)
     return F.linear(y.transpose(1, 2), out_proj_weight, out_proj_bias)

@@ -138,3 +138,38 @@ def test_mamba_inner_bf16_config1_block_vs_oracle():
                              None, A.to(DEV), None, None, D.to(DEV), delta_bias=bias.to(DEV))
     assert out.dtype == torch.bfloat16
     assert_close(out, ref, 2e-2, 2e-2, "config-1 block out")
+
+
+@pytest.mark.parametrize("which", ["b", "c", "dt", "bcdt"])
+@pytest.mark.parametrize("checkpoint_lvl", [0, 1])
+def test_mamba_inner_rms_options(which, checkpoint_lvl):
+    """B / C / dt RMSNorm options of mamba_inner_fn (selective_scan_interface.py:521-532, 572-589).
+    Forward with random norm weights against the oracle; gradients with unit norm weights (the
+    reference's checkpoint_lvl=1 recompute normalises the saved B / C a second time, which is
+    the identity up to eps for unit weights) against autograd through the oracle, whose norm
+    passes gradients straight through as the reference's backward does."""
+    from motif_ssm import mamba_inner_fn
+    rec = torch.load(os.path.join(GOLD, "inner_small.pt"), weights_only=False)
+    inp = rec["inputs"]
+    n = inp["A"].shape[1]
+    d = inp["A"].shape[0]
+    g = torch.Generator().manual_seed(3)
+    rand_w = {"b": 1 + 0.3 * torch.randn(n, generator=g), "c": 1 + 0.3 * torch.randn(n, generator=g),
+              "dt": 1 + 0.3 * torch.randn(d, generator=g)}
+    names = ("b", "c", "dt") if which == "bcdt" else (which,)
+    args = ("xz", "conv1d_weight", "conv1d_bias", "x_proj_weight", "delta_proj_weight", "out_proj_weight",
+            "out_proj_bias")
+    for weights, check_grads in ((rand_w, False), ({k: torch.ones_like(v) for k, v in rand_w.items()}, True)):
+        kw = {f"{k}_rms_weight": weights[k] for k in names}
+        leaves = {k: v.clone().requires_grad_(True) for k, v in inp.items()}
+        ref = O.mamba_inner_ref(*(leaves[k] for k in args), leaves["A"], None, None, leaves["D"],
+                                delta_bias=leaves["delta_bias"], **kw)
+        dl = {k: v.to(DEV).clone().requires_grad_(True) for k, v in inp.items()}
+        out = mamba_inner_fn(*(dl[k] for k in args), dl["A"], None, None, dl["D"], delta_bias=dl["delta_bias"],
+                             checkpoint_lvl=checkpoint_lvl, **{k: v.to(DEV) for k, v in kw.items()})
+        assert_close(out, ref, 1e-3, 1e-3, f"{which} out")
+        if check_grads:
+            ref.backward(rec["dout"])
+            out.backward(rec["dout"].to(DEV))
+            for k in inp:
+                assert_close(dl[k].grad, leaves[k].grad, 1e-3, 1e-3, f"{which} d{k}")
