@@ -50,7 +50,6 @@ template <typename T> struct BwdSmemT {
     static constexpr bool kPrefetch = sizeof(T) == 2;
     using BCT = typename std::conditional<kPrefetch, T, float>::type;
     BCT BC[2][bwd::NS][bwd::CK];              // B, C of the chunk
-    float RED[2][bwd::W][2][bwd::CK];         // double-buffered per-state dB / dC partials
     float ACC[2][bwd::NS][bwd::CK];           // chunk accumulator of dB / dC
     float DHC[bwd::KMAX][bwd::W][bwd::NS];    // reverse-recurrence carry into the previous chunk
     float DAACC[bwd::KMAX][bwd::W][bwd::NS];  // dA accumulators
@@ -273,9 +272,14 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
 
             // Two states per iteration, interleaved through every phase, so each warp always
             // has two independent dependency chains in flight.  An odd dstate pads the last
-            // pair with a state whose A, B and C are zero (it contributes nothing).
+            // pair with a state whose A, B and C are zero (it contributes nothing), and pairs
+            // beyond dstate are such states entirely (A, B, C, x rows are staged as zero).  The W warps
+            // walk the state pairs in rotation (warp w takes pair (j + w) mod W at step j), so
+            // at every step each warp owns a different pair's rows of the chunk accumulator and
+            // adds its dB / dC partials there directly; one barrier per step hands the rows on.
 #pragma unroll 1
-            for (int n0 = 0; n0 < p.nblk; n0 += 2) {  // uniform over the CTA
+            for (int j = 0; j < W; ++j) {  // uniform over the CTA; pairs past nblk are all-zero
+                const int n0 = 2 * ((j + w) & (W - 1));
                 const bool has1 = n0 + 1 < p.nblk;
                 float An[2], A2[2], Pl[2];
                 f32x2 A2p[2], Anp[2];
@@ -403,35 +407,38 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
                     S.DHC[cg][w][n0] = carry[0];  // carries into the previous chunk
                     if (has1) S.DHC[cg][w][n0 + 1] = carry[1];
                 }
-                // per-step gradients, as pairs; dB / dC partials go to the CTA reduction
+                // per-step gradients, as pairs; dB / dC partials are added into this pair's rows
+                // of the chunk accumulator (no other warp touches them during this step)
                 f32x2 dA2[2] = {pack2(0.f, 0.f), pack2(0.f, 0.f)};
 #pragma unroll
                 for (int s = 0; s < 2; ++s) {
-                    float *rb = &S.RED[s][w][0][0];
 #pragma unroll
-                    for (int m = 0; m < 4; ++m) {
-                        const f32x2 pv = fma2(dtu2[m] ^ 0x8000000080000000ull, Bv[s][m], h2[s][m]);  // a_t h_{t-1}
-                        const f32x2 gv = mul2(dh2[s][m], pv);
-                        S1[m] = fma2(dh2[s][m], Bv[s][m], S1[m]);
-                        S2[m] = fma2(Anp[s], gv, S2[m]);
-                        dA2[s] = fma2(dtf2[m], gv, dA2[s]);
-                        const int pos = (m >> 1) * 128 + lane * 4 + (m & 1) * 2;
-                        *reinterpret_cast<f32x2 *>(rb + pos) = mul2(dh2[s][m], dtu2[m]);
-                        *reinterpret_cast<f32x2 *>(rb + CK + pos) = mul2(dog2[m], h2[s][m]);
-                    }
-                }
-                __syncthreads();
-                {
-                    const int q = tid >> 7, pp = (tid & 127) * 2;
+                    for (int hh = 0; hh < 2; ++hh) {
+                        float4 *ab = reinterpret_cast<float4 *>(&S.ACC[0][n0 + s][hh * 128 + lane * 4]);
+                        float4 *ac = reinterpret_cast<float4 *>(&S.ACC[1][n0 + s][hh * 128 + lane * 4]);
+                        const bool live = s == 0 || has1;
+                        float4 vb = live ? *ab : make_float4(0.f, 0.f, 0.f, 0.f);
+                        float4 vc = live ? *ac : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-                    for (int s = 0; s < 2; ++s) {
-                        if (s == 1 && !has1) break;
-                        f32x2 sum = pack2(0.f, 0.f);
-#pragma unroll
-                        for (int ww = 0; ww < W; ++ww)
-                            sum = add2(sum, *reinterpret_cast<const f32x2 *>(&S.RED[s][ww][q][pp]));
-                        f32x2 *acc = reinterpret_cast<f32x2 *>(&S.ACC[q][n0 + s][pp]);
-                        *acc = add2(*acc, sum);
+                        for (int mm = 0; mm < 2; ++mm) {
+                            const int m = 2 * hh + mm;
+                            const f32x2 pv = fma2(dtu2[m] ^ 0x8000000080000000ull, Bv[s][m], h2[s][m]);  // a_t h_{t-1}
+                            const f32x2 gv = mul2(dh2[s][m], pv);
+                            S1[m] = fma2(dh2[s][m], Bv[s][m], S1[m]);
+                            S2[m] = fma2(Anp[s], gv, S2[m]);
+                            dA2[s] = fma2(dtf2[m], gv, dA2[s]);
+                            const float2 pb = unpack2(mul2(dh2[s][m], dtu2[m]));
+                            const float2 pc = unpack2(mul2(dog2[m], h2[s][m]));
+                            if (mm == 0) {
+                                vb.x += pb.x; vb.y += pb.y; vc.x += pc.x; vc.y += pc.y;
+                            } else {
+                                vb.z += pb.x; vb.w += pb.y; vc.z += pc.x; vc.w += pc.y;
+                            }
+                        }
+                        if (live) {
+                            *ab = vb;
+                            *ac = vc;
+                        }
                     }
                 }
 #pragma unroll
@@ -442,7 +449,7 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
                     for (int off = 16; off > 0; off >>= 1) dAp += __shfl_xor_sync(FULL, dAp, off);
                     if (lane == 0 && (s == 0 || has1)) S.DAACC[cg][w][n0 + s] += dAp;
                 }
-                __syncthreads();  // RED is rewritten by the next pair
+                __syncthreads();  // the accumulator rows pass to the next warp
             }
             // ---- per-element epilogue
             {
