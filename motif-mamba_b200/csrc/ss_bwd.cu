@@ -414,11 +414,11 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
                 for (int s = 0; s < 2; ++s) {
 #pragma unroll
                     for (int hh = 0; hh < 2; ++hh) {
-                        float4 *ab = reinterpret_cast<float4 *>(&S.ACC[0][n0 + s][hh * 128 + lane * 4]);
-                        float4 *ac = reinterpret_cast<float4 *>(&S.ACC[1][n0 + s][hh * 128 + lane * 4]);
+                        ulonglong2 *ab = reinterpret_cast<ulonglong2 *>(&S.ACC[0][n0 + s][hh * 128 + lane * 4]);
+                        ulonglong2 *ac = reinterpret_cast<ulonglong2 *>(&S.ACC[1][n0 + s][hh * 128 + lane * 4]);
                         const bool live = s == 0 || has1;
-                        float4 vb = live ? *ab : make_float4(0.f, 0.f, 0.f, 0.f);
-                        float4 vc = live ? *ac : make_float4(0.f, 0.f, 0.f, 0.f);
+                        ulonglong2 vb = live ? *ab : make_ulonglong2(0ull, 0ull);
+                        ulonglong2 vc = live ? *ac : make_ulonglong2(0ull, 0ull);
 #pragma unroll
                         for (int mm = 0; mm < 2; ++mm) {
                             const int m = 2 * hh + mm;
@@ -427,12 +427,14 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
                             S1[m] = fma2(dh2[s][m], Bv[s][m], S1[m]);
                             S2[m] = fma2(Anp[s], gv, S2[m]);
                             dA2[s] = fma2(dtf2[m], gv, dA2[s]);
-                            const float2 pb = unpack2(mul2(dh2[s][m], dtu2[m]));
-                            const float2 pc = unpack2(mul2(dog2[m], h2[s][m]));
+                            const f32x2 pb = mul2(dh2[s][m], dtu2[m]);
+                            const f32x2 pc = mul2(dog2[m], h2[s][m]);
                             if (mm == 0) {
-                                vb.x += pb.x; vb.y += pb.y; vc.x += pc.x; vc.y += pc.y;
+                                vb.x = add2(vb.x, pb);
+                                vc.x = add2(vc.x, pc);
                             } else {
-                                vb.z += pb.x; vb.w += pb.y; vc.z += pc.x; vc.w += pc.y;
+                                vb.y = add2(vb.y, pb);
+                                vc.y = add2(vc.y, pc);
                             }
                         }
                         if (live) {
