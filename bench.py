@@ -350,28 +350,70 @@ def ssc_needs_split():
     return nb.value > 0
 
 
-def run_e2e(t, dout, dev, stream, world, selective_scan_fn, algo, steps, dist):
-    """selective_scan_fn (autograd) per step: pinned host inputs -> device, forward,
-    backward, all 8 gradients -> pinned host.  Timed with CUDA events, max over ranks."""
+def run_e2e(t, dout, dev, stream, world, selective_scan_fn, algo, steps, dist, n_sub=8):
+    """selective_scan_fn (autograd) per step with host buffers: pinned host inputs ->
+    device, forward, backward, all 8 gradients -> pinned host, timed with CUDA events
+    around the whole step, max over ranks.
+
+    The batch is processed as ``n_sub`` sub-batches through the same public call (the scan
+    is independent across batch rows), pipelined over three streams: the host-to-device
+    copy of sub-batch i+1 and the device-to-host copy of sub-batch i-1's gradients overlap
+    sub-batch i's forward + backward.  dA, dD and ddelta_bias (sums over the batch) are
+    accumulated on the device across the sub-batches and copied once per step."""
     keys = ("u", "delta", "A", "B", "C", "D", "z", "delta_bias")
+    per_row = ("u", "delta", "B", "C", "z")
+    shared = ("A", "D", "delta_bias")
     host = {k: t[k].cpu().pin_memory() for k in keys}
     host_dout = dout.cpu().pin_memory()
     dev_bufs = {k: torch.empty_like(t[k]) for k in keys}
     dev_dout = torch.empty_like(dout)
     host_grads = {k: torch.empty(t[k].shape, dtype=t[k].dtype).pin_memory() for k in keys}
+    dev_shared_grads = {k: torch.empty_like(t[k]) for k in shared}
     h2d = sum(v.numel() * v.element_size() for v in host.values()) + host_dout.numel() * host_dout.element_size()
     d2h = sum(v.numel() * v.element_size() for v in host_grads.values())
+    batch = t["u"].shape[0]
+    n_sub = max(1, min(n_sub, batch))
+    bounds = [(i * batch // n_sub, (i + 1) * batch // n_sub) for i in range(n_sub)]
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    done = [torch.cuda.Event() for _ in range(n_sub)]  # compute of sub-batch i finished (inputs free)
+    for e in done:
+        e.record(stream)
 
     def one():
-        for k in keys:
-            dev_bufs[k].copy_(host[k], non_blocking=True)
-        dev_dout.copy_(host_dout, non_blocking=True)
-        leaves = {k: dev_bufs[k].detach().requires_grad_(True) for k in keys}
-        out = selective_scan_fn(leaves["u"], leaves["delta"], leaves["A"], leaves["B"], leaves["C"], leaves["D"],
-                                z=leaves["z"], delta_bias=leaves["delta_bias"], delta_softplus=True)
-        out.backward(dev_dout)
-        for k in keys:
-            host_grads[k].copy_(leaves[k].grad, non_blocking=True)
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(done[-1])  # the previous step's last sub-batch no longer reads A, D, bias
+            for k in shared:
+                dev_bufs[k].copy_(host[k], non_blocking=True)
+        for i, (b0, b1) in enumerate(bounds):
+            ready = torch.cuda.Event()
+            with torch.cuda.stream(s_in):
+                s_in.wait_event(done[i])  # the previous step's compute of this slice is over
+                for k in per_row:
+                    dev_bufs[k][b0:b1].copy_(host[k][b0:b1], non_blocking=True)
+                dev_dout[b0:b1].copy_(host_dout[b0:b1], non_blocking=True)
+                ready.record(s_in)
+            stream.wait_event(ready)
+            leaves = {k: (dev_bufs[k][b0:b1] if k in per_row else dev_bufs[k]).detach().requires_grad_(True)
+                      for k in keys}
+            out = selective_scan_fn(leaves["u"], leaves["delta"], leaves["A"], leaves["B"], leaves["C"],
+                                    leaves["D"], z=leaves["z"], delta_bias=leaves["delta_bias"], delta_softplus=True)
+            out.backward(dev_dout[b0:b1])
+            for k in shared:
+                if i == 0:
+                    dev_shared_grads[k].copy_(leaves[k].grad)
+                else:
+                    dev_shared_grads[k].add_(leaves[k].grad)
+            done[i].record(stream)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(done[i])
+                for k in per_row:
+                    g = leaves[k].grad
+                    g.record_stream(s_out)
+                    host_grads[k][b0:b1].copy_(g, non_blocking=True)
+        with torch.cuda.stream(s_out):
+            for k in shared:
+                host_grads[k].copy_(dev_shared_grads[k], non_blocking=True)
+        stream.wait_stream(s_out)
 
     for _ in range(2):
         one()
@@ -380,6 +422,7 @@ def run_e2e(t, dout, dev, stream, world, selective_scan_fn, algo, steps, dist):
         dist.barrier()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record(stream)
+    s_in.wait_stream(stream)
     for _ in range(steps):
         one()
     e.record(stream)
@@ -390,7 +433,8 @@ def run_e2e(t, dout, dev, stream, world, selective_scan_fn, algo, steps, dist):
     ms = tt.item() / steps
     return {"value": algo * world / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms, "steps": steps,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "api": "motif_ssm.selective_scan_fn forward + autograd backward, pinned host buffers"}
+            "api": f"motif_ssm.selective_scan_fn forward + autograd backward on {n_sub} sub-batches, pinned host "
+                   "buffers, host-to-device / compute / device-to-host pipelined on three streams"}
 
 
 PREFILL = dict(n_layer=24, d_model=768, vocab=512, d_state=16, global_batch=16, seqlen=4096,
