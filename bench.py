@@ -56,6 +56,19 @@ def hbm_peak():
         return FALLBACK_HBM, "fallback"
 
 
+def ncu_inst(kernel):
+    """Warp-instructions per launch of `kernel` for this workload, from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "dram_traffic.txt")
+    try:
+        for line in open(p):
+            parts = line.split()
+            if len(parts) >= 3 and parts[0] == kernel + ".inst" and parts[1] == "config4_l4096":
+                return int(float(parts[2]))
+    except OSError:
+        pass
+    return None
+
+
 def ncu_traffic(kernel):
     """DRAM bytes per launch of `kernel` for this workload, from the committed ncu summary."""
     p = os.path.join(ROOT, "profiles", "dram_traffic.txt")
@@ -327,7 +340,8 @@ def main():
                                    "frac_of_hbm": bwd_b / (bwd_ms * 1e-3) / 1e9 / peak}},
             "roofline": {"bound": "hbm", "kernel": dom_name, "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
-                         if peak_kind == "measured" else "fallback 6650 GB/s", "traffic": traffic},
+                         if peak_kind == "measured" else "fallback 6650 GB/s", "traffic": traffic,
+                         "issue": issue_ceiling(dom_name, dom_ms, clocks)},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
             "e2e": e2e,
@@ -348,6 +362,21 @@ def ssc_needs_split():
     nb = ctypes.c_int64(0)
     _lib.check(_lib.lib.ss_fwd_workspace_size(ctypes.byref(a), ctypes.byref(nb)))
     return nb.value > 0
+
+
+def issue_ceiling(kernel, ms, clocks):
+    """The ceiling that binds these kernels: warp-instruction issue.  Instructions per launch
+    come from the committed ncu capture (scaled with seqlen like the traffic); the peak is
+    4 warp-instructions per SM per clock (one per scheduler) x 148 SMs at the SM clock
+    sampled under load during the timed region."""
+    inst = ncu_inst(kernel)
+    if inst is None:
+        return None
+    mhz = (clocks or {}).get("sm_mhz") or 1965.0
+    achieved = inst / (ms * 1e-3) / 1e9
+    peak = 4 * 148 * mhz * 1e6 / 1e9
+    return {"warp_inst_per_launch": inst, "achieved": achieved, "peak": peak, "unit": "G warp-inst/s",
+            "frac": achieved / peak}
 
 
 def run_e2e(t, dout, dev, stream, world, selective_scan_fn, algo, steps, dist, n_sub=8):
