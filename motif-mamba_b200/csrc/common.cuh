@@ -32,6 +32,10 @@ template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float
 // p must be 16-byte aligned (8 x 16-bit = 16 B; 8 x fp32 = 2 x 16 B).
 template <typename T> struct Vec8;
 template <> struct Vec8<float> {
+    static __device__ __forceinline__ void load_rounded(const float (&v)[8], float (&r)[8]) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) r[i] = v[i];
+    }
     static __device__ __forceinline__ void load(const float *p, float (&v)[8]) {
         float4 a = reinterpret_cast<const float4 *>(p)[0];
         float4 b = reinterpret_cast<const float4 *>(p)[1];
@@ -44,6 +48,11 @@ template <> struct Vec8<float> {
     }
 };
 template <> struct Vec8<__nv_bfloat16> {
+    // v rounded to bf16 and back (the value a store followed by a load would give)
+    static __device__ __forceinline__ void load_rounded(const float (&v)[8], float (&r)[8]) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) r[i] = __bfloat162float(__float2bfloat16_rn(v[i]));
+    }
     static __device__ __forceinline__ void load(const __nv_bfloat16 *p, float (&v)[8]) {
         uint4 r = *reinterpret_cast<const uint4 *>(p);
         uint32_t w[4] = {r.x, r.y, r.z, r.w};
@@ -66,6 +75,10 @@ template <> struct Vec8<__nv_bfloat16> {
     }
 };
 template <> struct Vec8<__half> {
+    static __device__ __forceinline__ void load_rounded(const float (&v)[8], float (&r)[8]) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) r[i] = __half2float(__float2half_rn(v[i]));
+    }
     static __device__ __forceinline__ void load(const __half *p, float (&v)[8]) {
         uint4 r = *reinterpret_cast<const uint4 *>(p);
         uint32_t w[4] = {r.x, r.y, r.z, r.w};

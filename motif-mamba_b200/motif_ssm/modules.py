@@ -145,6 +145,20 @@ class Mambamotif(nn.Module):
         for p in (self.P, self.Q, self.pq_k):
             p.requires_grad_(True)
 
+    def _decode_consts(self):
+        """A = -exp(A_log) and the fp32 dt bias for decode steps, recomputed only when
+        A_log or the bias change (tracked by their version counters and storage), so a
+        decode step does not launch two elementwise kernels and a cast per layer for them.
+        A CUDA graph captured over ``step`` reads these cached tensors: in-place edits of
+        A_log / dt_proj.bias after capture need a new capture."""
+        key = (self.A_log._version, self.A_log.data_ptr(), self.dt_proj.bias._version,
+               self.dt_proj.bias.data_ptr())
+        if getattr(self, "_dc_key", None) != key:
+            with torch.no_grad():
+                self._dc = (-torch.exp(self.A_log.float()), self.dt_proj.bias.float().contiguous())
+            self._dc_key = key
+        return self._dc
+
     def _P_eff(self):
         return None if self.P is None else self.pq_k * self.P
 
@@ -200,8 +214,8 @@ class Mambamotif(nn.Module):
         x_db = self.x_proj(x)
         dt, B, C = torch.split(x_db, [self.dt_rank, self.d_state, self.d_state], dim=-1)
         dt = F.linear(dt, self.dt_proj.weight)
-        A = -torch.exp(self.A_log.float())
         if self.P is not None:
+            A = -torch.exp(self.A_log.float())
             dt = F.softplus(dt + self.dt_proj.bias.to(dtype=dt.dtype))
             y, last_state = selective_scan_fn(x.unsqueeze(-1), dt.unsqueeze(-1), A, B.unsqueeze(-1),
                                               C.unsqueeze(-1), D=self.D.float(), z=z.unsqueeze(-1),
@@ -209,8 +223,8 @@ class Mambamotif(nn.Module):
                                               P=self._P_eff(), Q=self.Q)
             ssm_state.copy_(last_state.to(ssm_state.dtype))
             return self.out_proj(y[..., 0]).unsqueeze(1), conv_state, ssm_state
-        y = selective_state_update(ssm_state, x, dt, A, B, C, self.D, z=z, dt_bias=self.dt_proj.bias,
-                                   dt_softplus=True)
+        A, dt_bias = self._decode_consts()
+        y = selective_state_update(ssm_state, x, dt, A, B, C, self.D, z=z, dt_bias=dt_bias, dt_softplus=True)
         return self.out_proj(y).unsqueeze(1), conv_state, ssm_state
 
     def allocate_inference_cache(self, batch_size, max_seqlen, dtype=None, **kwargs):
