@@ -55,6 +55,7 @@ template <typename T> struct BwdSmemT {
     float DAACC[bwd::KMAX][bwd::W][bwd::NS];  // dA accumulators
     float PBD[bwd::KMAX][bwd::W][2];          // dD, ddelta_bias accumulators
     float AX[bwd::W][2][bwd::NS];             // this pass's A row and chunk-start states, per warp
+    float AXP[2][bwd::W][3 * bwd::NS];        // prefetched A row and raw x pairs, by pass parity
     T PF[kPrefetch ? bwd::W : 1][5][bwd::CK]; // next pass's u, delta, dout, z, out (lane slices)
 };
 
@@ -148,9 +149,14 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
                             HAS_Z ? reinterpret_cast<const T *>(p.out) + (int64_t)b * p.out_bs : nullptr};
     const int64_t arr_ds[5] = {p.u_ds, p.delta_ds, p.dout_ds, p.z_ds, p.out_ds};
     constexpr int NARR = HAS_Z ? 5 : 3;
-    auto prefetch = [&](int kk, int cgg) {
+    // The A row and the chunk-start states (16 states, dense 16-byte-aligned rows) come the
+    // same way: lanes 0-3 copy A, lanes 4-11 the (decay, state) pairs of the previous chunk.
+    const bool axpf = pf && p.nblk == NS && p.A_ns == 1 && (p.A_ds & 3) == 0 &&
+                      (reinterpret_cast<uintptr_t>(p.A) & 15) == 0 && (p.state_lo & 1) == 0 && (p.dstate & 1) == 0;
+    auto prefetch = [&](int kk, int cgg, int par) {
         const int cin = (tile * K + cgg) * W + w;
-        const int dd = g * p.dpg + (cin < p.dpg ? cin : 0);
+        const bool cv = cin < p.dpg;
+        const int dd = g * p.dpg + (cv ? cin : 0);
         const int64_t tt = (int64_t)kk * CK + lane * IT;
         const int nb = (int)max((int64_t)0, min((int64_t)IT, L - tt)) * (int)sizeof(T);
 #pragma unroll
@@ -158,9 +164,23 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
             const T *src = arr_base[a] + (int64_t)dd * arr_ds[a] + (nb > 0 ? tt : 0);
             cp_async16(&S.PF[Smem::kPrefetch ? w : 0][a][lane * IT], src, nb);
         }
+        if (axpf && lane < 12) {
+            const float *src;
+            int nbx;
+            if (lane < 4) {
+                src = p.A + (int64_t)dd * p.A_ds + p.state_lo + 4 * lane;
+                nbx = cv ? 16 : 0;
+            } else {
+                const int64_t rw = (int64_t)b * p.dim + dd;
+                src = p.x + (rw * p.n_chunks + (kk > 0 ? kk - 1 : 0)) * 2 * p.dstate + 2 * p.state_lo + 4 * (lane - 4);
+                nbx = (cv && kk > 0) ? 16 : 0;
+            }
+            cp_async16(&S.AXP[par][w][4 * lane], src, nbx);
+        }
         cp_async_commit();
     };
-    if (pf && p.n_chunks > 0) prefetch(p.n_chunks - 1, 0);
+    if (pf && p.n_chunks > 0) prefetch(p.n_chunks - 1, 0, 0);
+    int pass = 0;
 
     for (int k = p.n_chunks - 1; k >= 0; --k) {
         const int64_t kt0 = (int64_t)k * CK;
@@ -204,8 +224,8 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
                         Vec8<T>::load(pw + 4 * CK, ov);
                     }
                     __syncwarp();
-                    if (cg + 1 < K) prefetch(k, cg + 1);
-                    else if (k > 0) prefetch(k - 1, 0);
+                    if (cg + 1 < K) prefetch(k, cg + 1, (pass + 1) & 1);
+                    else if (k > 0) prefetch(k - 1, 0, (pass + 1) & 1);
                 } else {
                     load_items(arr_base[0] + (int64_t)d * p.u_ds, t0, L, vec, uf);
                     load_items(arr_base[1] + (int64_t)d * p.delta_ds, t0, L, vec, dv);
@@ -261,7 +281,12 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
             for (int m = 0; m < 4; ++m) S1[m] = S2[m] = pack2(0.f, 0.f);
             // A row and the chunk-start states of this channel, read once per pass (off the
             // per-state dependency chain)
-            if (lane < NS) {  // states >= dstate read as zero (A, state), like their zero B / C rows
+            if (axpf) {
+                if (lane < NS) {
+                    S.AX[w][0][lane] = S.AXP[pass & 1][w][lane];
+                    S.AX[w][1][lane] = S.AXP[pass & 1][w][NS + 2 * lane + 1];
+                }
+            } else if (lane < NS) {  // states >= dstate read as zero (A, state), like their zero B / C rows
                 const bool st = valid && lane < p.nblk;
                 const int ng = p.state_lo + lane;
                 S.AX[w][0][lane] = st ? p.A[(int64_t)d * p.A_ds + (int64_t)ng * p.A_ns] : 0.f;
@@ -522,6 +547,7 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
                 }
             }
             __syncthreads();
+            ++pass;
         }
         // ---- flush the chunk's dB / dC (summed over this CTA's channels)
         __syncthreads();
