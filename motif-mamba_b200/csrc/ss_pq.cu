@@ -5,19 +5,24 @@
 // (reference: selective_scan_ref with P/Q, mamba_ssm/ops/selective_scan_interface.py:402-433;
 // full-matrix path :262-350).  P is (dstate, r) shared or (dim, dstate, r) per channel, Q is
 // (r, dstate) or (dim, r, dstate), r <= 8, dstate <= 16.  The coupling mixes states, so the
-// diagonal-scan tricks of ss_fwd / ss_bwd do not apply: one thread owns one channel and
-// walks the sequence with all 16 states in registers.
+// diagonal-scan tricks of ss_fwd / ss_bwd do not apply and time stays sequential per channel.
+// To give the GPU enough warps, a channel's 16 states are split over a quad of 4 adjacent
+// lanes (4 states each): per step q = Q h is a quad sum (two shuffles per rank), pq = P q,
+// the diagonal update and the output's quad sum.  Each lane keeps its slice of P and Q in
+// registers (rows n of P, columns n of Q for its 4 states), and in the backward also its
+// slice of dP and dQ, so nothing is accumulated through shared memory per step.
 //
-// Forward: per step q = Q h (r x 16 FMAs), pq = P q, the diagonal update, y = <C, h>, the
-// D-skip and z gate; B/C tiles are staged in shared memory, u/delta/z rows are read by their
-// owning thread with 16-byte loads; x gets the state every 256 steps as in ss_fwd.
+// Forward: B/C tiles of 32 steps are staged in shared memory for the CTA's 32 channels;
+// u/delta/z rows are read by the channel's quad with 16-byte loads; x gets the state every
+// 256 steps as in ss_fwd.
 // Backward (O(L)): a forward sweep stores the state at every 16-step segment start in a
 // workspace; then segments are processed in reverse: the 16 states of each step are
 // recomputed into shared memory and the adjoint g_t = C_t doutg_t + M_{t+1}^T g_{t+1}
-// (M = diag(a) + dt P Q, M^T g = a g + dt Q^T (P^T g)) runs backwards, accumulating
-// du, ddelta, dA, dD, ddelta_bias, dP = sum dt g (Q h_{t-1})^T, dQ = sum dt (P^T g) h_{t-1}^T;
-// dB / dC are summed over the warp's 32 channels through a shared-memory transpose and
-// added once per lane with an fp32 atomic into the same accumulators ss_bwd uses.
+// (M = diag(a) + dt P Q, M^T g = a g + dt Q^T (P^T g)) runs backwards, accumulating du,
+// ddelta, dA, dD, ddelta_bias, dP = sum dt g (Q h_prev)^T and dQ = sum dt (P^T g) h_prev^T.
+// dB / dC (sums over channels) are reduce-scattered over the warp's 8 channels with
+// shuffles, summed over the CTA's 4 warps per segment in shared memory, and added to the
+// fp32 accumulators with one vector atomic per thread and segment.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -25,10 +30,10 @@ namespace mss {
 
 namespace pq {
 constexpr int NS = 16;   // states (dstate <= 16, zero padded)
-constexpr int RM = 8;    // max rank
+constexpr int SPT = 4;   // states per lane (a quad of lanes per channel)
+constexpr int NT = 128;  // threads per CTA = 32 channels
+constexpr int CH = NT / 4;
 constexpr int TT = 32;   // forward tile (divides the 256-step x chunk)
-constexpr int CHF = 64;  // forward channels per CTA
-constexpr int CHB = 32;  // backward channels per CTA (one warp)
 constexpr int SEG = 16;  // backward segment length
 }  // namespace pq
 
@@ -51,52 +56,73 @@ __device__ __forceinline__ void pq_store8(T *row, int64_t t0, int64_t L, bool ve
             if (t0 + i < L) row[t0 + i] = from_f<T>(v[i]);
     }
 }
+__device__ __forceinline__ float quad_sum(float v) {
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    return v + __shfl_xor_sync(0xffffffffu, v, 2);
+}
 
-// Fill P (index n*RM+k) and Q (index k*NS+n) into shared memory, zero-padded to NS x RM.
-// Per-channel layout is [index][thread] (conflict-free); shared layout is [index].
-template <bool PER_DIM, int CH>
-__device__ __forceinline__ void pq_fill(float *Pm, float *Qm, const float *P, const float *Q, int d, bool valid,
-                                        int dstate, int r, int tid) {
-    using namespace pq;
-    if constexpr (PER_DIM) {
-        for (int idx = 0; idx < NS * RM; ++idx) {
-            const int n = idx / RM, k = idx - n * RM;
-            Pm[idx * CH + tid] = (valid && n < dstate && k < r) ? P[((int64_t)d * dstate + n) * r + k] : 0.f;
-            const int k2 = idx / NS, n2 = idx - k2 * NS;
-            Qm[idx * CH + tid] = (valid && n2 < dstate && k2 < r) ? Q[((int64_t)d * r + k2) * dstate + n2] : 0.f;
-        }
-    } else {
-        for (int idx = tid; idx < NS * RM; idx += CH) {
-            const int n = idx / RM, k = idx - n * RM;
-            Pm[idx] = (n < dstate && k < r) ? P[n * r + k] : 0.f;
-            const int k2 = idx / NS, n2 = idx - k2 * NS;
-            Qm[idx] = (n2 < dstate && k2 < r) ? Q[k2 * dstate + n2] : 0.f;
+// This lane's slice of P (rows n = 4 qt + j) and Q (columns n), zero beyond dstate / r.
+template <int RM>
+__device__ __forceinline__ void load_pq_slice(const float *P, const float *Q, bool per_dim, int64_t d, int dstate,
+                                              int r, int qt, bool valid, float (&Pr)[pq::SPT][RM],
+                                              float (&Qr)[RM][pq::SPT]) {
+    const float *Pb = per_dim ? P + d * dstate * r : P;
+    const float *Qb = per_dim ? Q + d * r * dstate : Q;
+#pragma unroll
+    for (int j = 0; j < pq::SPT; ++j) {
+        const int n = pq::SPT * qt + j;
+#pragma unroll
+        for (int k = 0; k < RM; ++k) {
+            const bool ok = valid && n < dstate && k < r;
+            Pr[j][k] = ok ? Pb[n * r + k] : 0.f;
+            Qr[k][j] = ok ? Qb[k * dstate + n] : 0.f;
         }
     }
 }
 
-template <typename T, bool HAS_Z, bool PER_DIM>
-__global__ void __launch_bounds__(pq::CHF) ss_pq_fwd_kernel(const FwdParams p) {
+// One step of the coupled recurrence for this lane's 4 states (h holds h_{t-1} on entry).
+template <int RM>
+__device__ __forceinline__ void pq_step(float (&h)[pq::SPT], const float (&Pr)[pq::SPT][RM],
+                                        const float (&Qr)[RM][pq::SPT], const float (&A2)[pq::SPT], float dt,
+                                        float dtu, const float *bt) {
+    float q[RM];
+#pragma unroll
+    for (int k = 0; k < RM; ++k) {
+        float s = 0.f;
+#pragma unroll
+        for (int j = 0; j < pq::SPT; ++j) s = fmaf(Qr[k][j], h[j], s);
+        q[k] = quad_sum(s);
+    }
+#pragma unroll
+    for (int j = 0; j < pq::SPT; ++j) {
+        float pqn = 0.f;
+#pragma unroll
+        for (int k = 0; k < RM; ++k) pqn = fmaf(Pr[j][k], q[k], pqn);
+        h[j] = fmaf(ex2(dt * A2[j]), h[j], fmaf(dt, pqn, dtu * bt[j]));
+    }
+}
+
+template <typename T, bool HAS_Z, int RM>
+__global__ void __launch_bounds__(pq::NT) ss_pq_fwd_kernel(const FwdParams p) {
     using namespace pq;
-    constexpr int CH = CHF, PW = PER_DIM ? CH : 1;
-    extern __shared__ __align__(16) float sm[];
-    float *Bs = sm, *Cs = Bs + TT * NS, *Pm = Cs + TT * NS, *Qm = Pm + NS * RM * PW;
-    const int tid = threadIdx.x, pi = PER_DIM ? tid : 0;
+    __shared__ __align__(16) float Bs[TT][NS], Cs[TT][NS];
+    const int tid = threadIdx.x, ch = tid >> 2, qt = tid & 3;
     const int g = blockIdx.x / p.tiles_per_group, tile = blockIdx.x - g * p.tiles_per_group;
     const int b = blockIdx.y;
-    const int cin = tile * CH + tid;
+    const int cin = tile * CH + ch;
     const bool valid = cin < p.dpg;
     const int d = g * p.dpg + (valid ? cin : 0);
     const int64_t L = p.seqlen, row = (int64_t)b * p.dim + d;
     const bool vec = p.aligned != 0;
     const int r = p.pq_rank;
-    pq_fill<PER_DIM, CH>(Pm, Qm, p.P, p.Q, d, valid, p.dstate, r, tid);
-
-    float A2[NS], h[NS];
+    float Pr[SPT][RM], Qr[RM][SPT];
+    load_pq_slice<RM>(p.P, p.Q, p.pq_per_dim != 0, d, p.dstate, r, qt, valid, Pr, Qr);
+    float A2[SPT], h[SPT];
 #pragma unroll
-    for (int n = 0; n < NS; ++n) {
-        A2[n] = (valid && n < p.dstate) ? p.A[(int64_t)d * p.A_ds + (int64_t)n * p.A_ns] * kLog2e : 0.f;
-        h[n] = 0.f;
+    for (int j = 0; j < SPT; ++j) {
+        const int n = SPT * qt + j;
+        A2[j] = (valid && n < p.dstate) ? p.A[(int64_t)d * p.A_ds + (int64_t)n * p.A_ns] * kLog2e : 0.f;
+        h[j] = 0.f;
     }
     const float Dv = (p.D && valid) ? p.D[(int64_t)d * p.D_s] : 0.f;
     const float bias = (p.delta_bias && valid) ? p.delta_bias[(int64_t)d * p.delta_bias_s] : 0.f;
@@ -111,11 +137,11 @@ __global__ void __launch_bounds__(pq::CHF) ss_pq_fwd_kernel(const FwdParams p) {
 
     for (int64_t t0 = 0; t0 < L; t0 += TT) {
         __syncthreads();
-        for (int i = tid; i < TT * NS; i += CH) {
+        for (int i = tid; i < TT * NS; i += NT) {
             const int t = i / NS, n = i - t * NS;
             const bool ok = t0 + t < L && n < p.dstate;
-            Bs[i] = ok ? to_f<T>(gB[(int64_t)n * p.B_ns + t0 + t]) : 0.f;
-            Cs[i] = ok ? to_f<T>(gC[(int64_t)n * p.C_ns + t0 + t]) : 0.f;
+            Bs[t][n] = ok ? to_f<T>(gB[(int64_t)n * p.B_ns + t0 + t]) : 0.f;
+            Cs[t][n] = ok ? to_f<T>(gC[(int64_t)n * p.C_ns + t0 + t]) : 0.f;
         }
         __syncthreads();
 #pragma unroll 1
@@ -124,36 +150,20 @@ __global__ void __launch_bounds__(pq::CHF) ss_pq_fwd_kernel(const FwdParams p) {
             float uf[8], dv[8], y[8];
             pq_load8(ur, tg, L, vec, uf);
             pq_load8(dr, tg, L, vec, dv);
-#pragma unroll 1
+#pragma unroll
             for (int j = 0; j < 8; ++j) {
                 float dt = dv[j] + bias;
                 if (p.softplus) dt = softplus20(dt);
                 dt = (valid && tg + j < L) ? dt : 0.f;
                 cum += dt;
-                const float dtu = dt * uf[j];
-                float q[RM];
+                const float *bt = &Bs[g8 + j][SPT * qt], *ct = &Cs[g8 + j][SPT * qt];
+                pq_step<RM>(h, Pr, Qr, A2, dt, dt * uf[j], bt);
+                float yp = 0.f;
 #pragma unroll
-                for (int k = 0; k < RM; ++k) {
-                    q[k] = 0.f;
-                    if (k < r) {
-#pragma unroll
-                        for (int n = 0; n < NS; ++n) q[k] = fmaf(Qm[(k * NS + n) * PW + pi], h[n], q[k]);
-                    }
-                }
-                const float *bt = Bs + (g8 + j) * NS, *ct = Cs + (g8 + j) * NS;
-                float acc = 0.f;
-#pragma unroll
-                for (int n = 0; n < NS; ++n) {
-                    float pqn = 0.f;
-#pragma unroll
-                    for (int k = 0; k < RM; ++k)
-                        if (k < r) pqn = fmaf(Pm[(n * RM + k) * PW + pi], q[k], pqn);
-                    h[n] = fmaf(ex2(dt * A2[n]), h[n], fmaf(dt, pqn, dtu * bt[n]));
-                    acc = fmaf(ct[n], h[n], acc);
-                }
-                y[j] = fmaf(Dv, uf[j], acc);
+                for (int k = 0; k < SPT; ++k) yp = fmaf(ct[k], h[k], yp);
+                y[j] = fmaf(Dv, uf[j], quad_sum(yp));
             }
-            if (valid) {
+            if (valid && qt == 0) {
                 pq_store8(orow, tg, L, vec, y);
                 if constexpr (HAS_Z) {
                     float zf[8];
@@ -168,57 +178,61 @@ __global__ void __launch_bounds__(pq::CHF) ss_pq_fwd_kernel(const FwdParams p) {
         if (valid && (te % kChunkLen == 0 || te == L)) {
             float *xr = p.x + (row * p.n_chunks + (te - 1) / kChunkLen) * 2 * p.dstate;
 #pragma unroll
-            for (int n = 0; n < NS; ++n)
+            for (int j = 0; j < SPT; ++j) {
+                const int n = SPT * qt + j;
                 if (n < p.dstate) {
-                    xr[2 * n] = ex2(A2[n] * cum);
-                    xr[2 * n + 1] = h[n];
+                    xr[2 * n] = ex2(A2[j] * cum);
+                    xr[2 * n + 1] = h[j];
                 }
+            }
         }
     }
 }
 
-template <typename T, bool HAS_Z, bool PER_DIM>
-struct PqBwdLayout {
-    static constexpr int PW = PER_DIM ? pq::CHB : 1;
-    static constexpr int P_OFF = 0, Q_OFF = P_OFF + pq::NS * pq::RM * PW;
-    static constexpr int DP_OFF = Q_OFF + pq::NS * pq::RM * PW;                 // [idx][lane]
-    static constexpr int DQ_OFF = DP_OFF + pq::NS * pq::RM * pq::CHB;
-    static constexpr int HS_OFF = DQ_OFF + pq::NS * pq::RM * pq::CHB;            // [SEG+1][NS][lane]
-    static constexpr int SV_OFF = HS_OFF + (pq::SEG + 1) * pq::NS * pq::CHB;     // [5][SEG][lane]
-    static constexpr int BS_OFF = SV_OFF + 5 * pq::SEG * pq::CHB;                // B, C [SEG][NS]
-    static constexpr int RD_OFF = BS_OFF + 2 * pq::SEG * pq::NS;                 // [32][33]
-    static constexpr int FLOATS = RD_OFF + 32 * 33;
+struct PqBwdSmem {
+    float HS[pq::SEG + 1][pq::NT][pq::SPT];  // states of the segment, per lane
+    float Bs[pq::SEG][pq::NS], Cs[pq::SEG][pq::NS];
+    float SV[5][pq::SEG][pq::CH];            // per channel and step: u, dt, dt u, doutg, gate
+    float DU[pq::SEG][pq::CH], DD[pq::SEG][pq::CH];
+    float WACC[pq::NT / 32][pq::SEG][32];    // warp sums of dB / dC per step
 };
 
-template <typename T, bool HAS_Z, bool PER_DIM>
-__global__ void __launch_bounds__(pq::CHB) ss_pq_bwd_kernel(const BwdParams p) {
+template <typename T, bool HAS_Z, int RM>
+__global__ void __launch_bounds__(pq::NT) ss_pq_bwd_kernel(const BwdParams p) {
     using namespace pq;
-    using Ly = PqBwdLayout<T, HAS_Z, PER_DIM>;
-    constexpr int PW = Ly::PW;
-    extern __shared__ __align__(16) float sm[];
-    float *Pm = sm + Ly::P_OFF, *Qm = sm + Ly::Q_OFF, *dPm = sm + Ly::DP_OFF, *dQm = sm + Ly::DQ_OFF;
-    float *HS = sm + Ly::HS_OFF, *SV = sm + Ly::SV_OFF, *Bs = sm + Ly::BS_OFF, *Cs = Bs + SEG * NS;
-    float *RD = sm + Ly::RD_OFF;
-    float *SU = SV, *SDT = SV + SEG * CHB, *SDU = SV + 2 * SEG * CHB, *SDG = SV + 3 * SEG * CHB,
-          *SGT = SV + 4 * SEG * CHB;  // u, dt, dt*u, doutg, softplus gate: [SEG][lane]
-    const int lane = threadIdx.x, pi = PER_DIM ? lane : 0;
+    constexpr int NW = NT / 32;
+    extern __shared__ __align__(16) char pq_smem[];
+    PqBwdSmem &S = *reinterpret_cast<PqBwdSmem *>(pq_smem);
+    auto &HS = S.HS;
+    auto &Bs = S.Bs;
+    auto &Cs = S.Cs;
+    auto &SV = S.SV;
+    auto &DU = S.DU;
+    auto &DD = S.DD;
+    auto &WACC = S.WACC;
+    float(&SU)[SEG][CH] = SV[0];
+    float(&SDT)[SEG][CH] = SV[1];
+    float(&SDTU)[SEG][CH] = SV[2];
+    float(&SDG)[SEG][CH] = SV[3];
+    float(&SGT)[SEG][CH] = SV[4];
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, ch = tid >> 2, qt = tid & 3;
     const int g = blockIdx.x / p.tiles_per_group, tile = blockIdx.x - g * p.tiles_per_group;
     const int b = blockIdx.y;
-    const int cin = tile * CHB + lane;
+    const int cin = tile * CH + ch;
     const bool valid = cin < p.dpg;
     const int d = g * p.dpg + (valid ? cin : 0);
     const int64_t L = p.seqlen, row = (int64_t)b * p.dim + d;
     const bool vec = p.aligned != 0;
     const int r = p.pq_rank;
     const int nseg = (int)((L + SEG - 1) / SEG);
-    pq_fill<PER_DIM, CHB>(Pm, Qm, p.P, p.Q, d, valid, p.dstate, r, lane);
-    for (int i = lane; i < NS * RM * CHB; i += CHB) dPm[i] = dQm[i] = 0.f;
-
-    float A2[NS], An[NS];
+    float Pr[SPT][RM], Qr[RM][SPT];
+    load_pq_slice<RM>(p.P, p.Q, p.pq_per_dim != 0, d, p.dstate, r, qt, valid, Pr, Qr);
+    float A2[SPT], An[SPT];
 #pragma unroll
-    for (int n = 0; n < NS; ++n) {
-        An[n] = (valid && n < p.dstate) ? p.A[(int64_t)d * p.A_ds + (int64_t)n * p.A_ns] : 0.f;
-        A2[n] = An[n] * kLog2e;
+    for (int j = 0; j < SPT; ++j) {
+        const int n = SPT * qt + j;
+        An[j] = (valid && n < p.dstate) ? p.A[(int64_t)d * p.A_ds + (int64_t)n * p.A_ns] : 0.f;
+        A2[j] = An[j] * kLog2e;
     }
     const float Dv = (p.D && valid) ? p.D[(int64_t)d * p.D_s] : 0.f;
     const float bias = (p.delta_bias && valid) ? p.delta_bias[(int64_t)d * p.delta_bias_s] : 0.f;
@@ -227,38 +241,20 @@ __global__ void __launch_bounds__(pq::CHB) ss_pq_bwd_kernel(const BwdParams p) {
     const T *dor = reinterpret_cast<const T *>(p.dout) + (int64_t)b * p.dout_bs + (int64_t)d * p.dout_ds;
     const T *gB = reinterpret_cast<const T *>(p.B) + (int64_t)b * p.B_bs + (int64_t)g * p.B_gs;
     const T *gC = reinterpret_cast<const T *>(p.C) + (int64_t)b * p.C_bs + (int64_t)g * p.C_gs;
-    float *ck = p.ckpt + row * (int64_t)nseg * NS;
+    float *ck = p.ckpt + row * (int64_t)nseg * NS + SPT * qt;
 
-    auto stage_bc = [&](int64_t t0) {
-        __syncwarp();
-        for (int i = lane; i < SEG * NS; i += CHB) {
+    auto stage_bc = [&](int64_t t0) {  // caller syncs
+        for (int i = tid; i < SEG * NS; i += NT) {
             const int t = i / NS, n = i - t * NS;
             const bool ok = t0 + t < L && n < p.dstate;
-            Bs[i] = ok ? to_f<T>(gB[(int64_t)n * p.B_ns + t0 + t]) : 0.f;
-            Cs[i] = ok ? to_f<T>(gC[(int64_t)n * p.C_ns + t0 + t]) : 0.f;
-        }
-        __syncwarp();
-    };
-    auto step_fwd = [&](float (&h)[NS], float dt, float dtu, const float *bt) {
-        float q[RM];
-#pragma unroll
-        for (int k = 0; k < RM; ++k) {
-            q[k] = 0.f;
-            if (k < r) {
-#pragma unroll
-                for (int n = 0; n < NS; ++n) q[k] = fmaf(Qm[(k * NS + n) * PW + pi], h[n], q[k]);
-            }
-        }
-#pragma unroll
-        for (int n = 0; n < NS; ++n) {
-            float pqn = 0.f;
-#pragma unroll
-            for (int k = 0; k < RM; ++k)
-                if (k < r) pqn = fmaf(Pm[(n * RM + k) * PW + pi], q[k], pqn);
-            h[n] = fmaf(ex2(dt * A2[n]), h[n], fmaf(dt, pqn, dtu * bt[n]));
+            Bs[t][n] = ok ? to_f<T>(gB[(int64_t)n * p.B_ns + t0 + t]) : 0.f;
+            Cs[t][n] = ok ? to_f<T>(gC[(int64_t)n * p.C_ns + t0 + t]) : 0.f;
         }
     };
-    auto load_seg = [&](int64_t t0) {  // per-step inputs of this lane's row -> SV
+    // Per-step inputs of this channel for a segment (the quad's first lane computes them);
+    // with `full` also doutg, the z outputs and the softplus gate.
+    auto load_seg = [&](int64_t t0, bool full) {
+        if (qt != 0) return;
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
             float uf[8], dv[8];
@@ -274,44 +270,12 @@ __global__ void __launch_bounds__(pq::CHB) ss_pq_bwd_kernel(const BwdParams p) {
                     x = softplus20(x);
                 }
                 x = (valid && t0 + t < L) ? x : 0.f;
-                SU[t * CHB + lane] = uf[j];
-                SDT[t * CHB + lane] = x;
-                SDU[t * CHB + lane] = x * uf[j];
-                SGT[t * CHB + lane] = gate;
+                SU[t][ch] = uf[j];
+                SDT[t][ch] = x;
+                SDTU[t][ch] = x * uf[j];
+                SGT[t][ch] = gate;
             }
-        }
-    };
-
-    // ---- forward sweep: the state at the start of every segment
-    {
-        float h[NS];
-#pragma unroll
-        for (int n = 0; n < NS; ++n) h[n] = 0.f;
-        for (int s = 0; s < nseg; ++s) {
-            const int64_t t0 = (int64_t)s * SEG;
-#pragma unroll
-            for (int n = 0; n < NS; ++n) ck[(int64_t)s * NS + n] = h[n];
-            stage_bc(t0);
-            load_seg(t0);
-            __syncwarp();
-            for (int t = 0; t < SEG && t0 + t < L; ++t)
-                step_fwd(h, SDT[t * CHB + lane], SDU[t * CHB + lane], Bs + t * NS);
-        }
-    }
-
-    // ---- reverse sweep over segments
-    float carry[NS], dA[NS];
-#pragma unroll
-    for (int n = 0; n < NS; ++n) carry[n] = dA[n] = 0.f;
-    float dDs = 0.f, dbs = 0.f;
-    for (int s = nseg - 1; s >= 0; --s) {
-        const int64_t t0 = (int64_t)s * SEG;
-        const int tv = (int)min((int64_t)SEG, L - t0);
-        stage_bc(t0);
-        load_seg(t0);
-        // doutg and the z gate outputs
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
+            if (!full) continue;
             float dov[8];
             pq_load8(dor, t0 + 8 * hh, L, vec, dov);
             if constexpr (HAS_Z) {
@@ -336,96 +300,128 @@ __global__ void __launch_bounds__(pq::CHB) ss_pq_bwd_kernel(const BwdParams p) {
                 }
             }
 #pragma unroll
-            for (int j = 0; j < 8; ++j) SDG[(8 * hh + j) * CHB + lane] = valid ? dov[j] : 0.f;
+            for (int j = 0; j < 8; ++j) SDG[8 * hh + j][ch] = valid ? dov[j] : 0.f;
         }
-        // states of the segment: HS[0] = h before it, HS[t+1] = h_t
-        {
-            float h[NS];
+    };
+
+    // ---- forward sweep: the state at the start of every segment
+    {
+        float h[SPT] = {0.f, 0.f, 0.f, 0.f};
+        for (int s = 0; s < nseg; ++s) {
+            const int64_t t0 = (int64_t)s * SEG;
+            if (valid)  // a lane of a padding channel aliases channel 0's row: it must not write
+                *reinterpret_cast<float4 *>(ck + (int64_t)s * NS) = make_float4(h[0], h[1], h[2], h[3]);
+            __syncthreads();
+            stage_bc(t0);
+            load_seg(t0, false);
+            __syncthreads();
+            const int tv = (int)min((int64_t)SEG, L - t0);
+            for (int t = 0; t < tv; ++t)
+                pq_step<RM>(h, Pr, Qr, A2, SDT[t][ch], SDTU[t][ch], &Bs[t][SPT * qt]);
+        }
+    }
+
+    // ---- reverse sweep over segments
+    float carry[SPT] = {0.f, 0.f, 0.f, 0.f}, dA[SPT] = {0.f, 0.f, 0.f, 0.f};
+    float dP[SPT][RM], dQ[RM][SPT];
 #pragma unroll
-            for (int n = 0; n < NS; ++n) {
-                h[n] = ck[(int64_t)s * NS + n];
-                HS[n * CHB + lane] = h[n];
-            }
-            __syncwarp();
+    for (int j = 0; j < SPT; ++j)
+#pragma unroll
+        for (int k = 0; k < RM; ++k) dP[j][k] = dQ[k][j] = 0.f;
+    float dDs = 0.f, dbs = 0.f;
+    for (int s = nseg - 1; s >= 0; --s) {
+        const int64_t t0 = (int64_t)s * SEG;
+        const int tv = (int)min((int64_t)SEG, L - t0);
+        __syncthreads();
+        stage_bc(t0);
+        load_seg(t0, true);
+        __syncthreads();
+        {  // states of the segment: HS[0] = h before it, HS[t+1] = h_t
+            const float4 c4 = valid ? *reinterpret_cast<const float4 *>(ck + (int64_t)s * NS)
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+            float h[SPT] = {c4.x, c4.y, c4.z, c4.w};
+            *reinterpret_cast<float4 *>(&HS[0][tid][0]) = c4;
             for (int t = 0; t < tv; ++t) {
-                step_fwd(h, SDT[t * CHB + lane], SDU[t * CHB + lane], Bs + t * NS);
-#pragma unroll
-                for (int n = 0; n < NS; ++n) HS[((t + 1) * NS + n) * CHB + lane] = h[n];
+                pq_step<RM>(h, Pr, Qr, A2, SDT[t][ch], SDTU[t][ch], &Bs[t][SPT * qt]);
+                *reinterpret_cast<float4 *>(&HS[t + 1][tid][0]) = make_float4(h[0], h[1], h[2], h[3]);
             }
         }
         for (int t = tv - 1; t >= 0; --t) {
-            const float dt = SDT[t * CHB + lane], uu = SU[t * CHB + lane], dg = SDG[t * CHB + lane];
-            const float *bt = Bs + t * NS, *ct = Cs + t * NS;
-            float gv[NS], hp[NS];
+            const float dt = SDT[t][ch], dtu = SDTU[t][ch], dg = SDG[t][ch];
+            const float4 hp4 = *reinterpret_cast<const float4 *>(&HS[t][tid][0]);
+            const float4 hn4 = *reinterpret_cast<const float4 *>(&HS[t + 1][tid][0]);
+            const float hp[SPT] = {hp4.x, hp4.y, hp4.z, hp4.w}, hn[SPT] = {hn4.x, hn4.y, hn4.z, hn4.w};
+            const float *bt = &Bs[t][SPT * qt], *ct = &Cs[t][SPT * qt];
+            float gv[SPT];
 #pragma unroll
-            for (int n = 0; n < NS; ++n) {
-                gv[n] = fmaf(dg, ct[n], carry[n]);
-                hp[n] = HS[(t * NS + n) * CHB + lane];
-            }
+            for (int j = 0; j < SPT; ++j) gv[j] = fmaf(dg, ct[j], carry[j]);
             float qh[RM], ptg[RM];
 #pragma unroll
             for (int k = 0; k < RM; ++k) {
-                qh[k] = ptg[k] = 0.f;
-                if (k < r) {
+                float s1 = 0.f, s2 = 0.f;
 #pragma unroll
-                    for (int n = 0; n < NS; ++n) {
-                        qh[k] = fmaf(Qm[(k * NS + n) * PW + pi], hp[n], qh[k]);
-                        ptg[k] = fmaf(Pm[(n * RM + k) * PW + pi], gv[n], ptg[k]);
-                    }
+                for (int j = 0; j < SPT; ++j) {
+                    s1 = fmaf(Qr[k][j], hp[j], s1);
+                    s2 = fmaf(Pr[j][k], gv[j], s2);
                 }
+                qh[k] = quad_sum(s1);
+                ptg[k] = quad_sum(s2);
             }
-            float S1 = 0.f, S2 = 0.f;
-            float red[2 * NS];
+            float S1 = 0.f, S2 = 0.f, red[2 * SPT];
 #pragma unroll
-            for (int n = 0; n < NS; ++n) {
-                const float a = ex2(dt * A2[n]);
+            for (int j = 0; j < SPT; ++j) {
+                const float a = ex2(dt * A2[j]);
                 float pqn = 0.f, qtp = 0.f;
 #pragma unroll
-                for (int k = 0; k < RM; ++k)
-                    if (k < r) {
-                        pqn = fmaf(Pm[(n * RM + k) * PW + pi], qh[k], pqn);
-                        qtp = fmaf(Qm[(k * NS + n) * PW + pi], ptg[k], qtp);
-                    }
-                const float ahp = a * hp[n];
-                S1 = fmaf(gv[n], bt[n], S1);
-                S2 = fmaf(gv[n], fmaf(An[n], ahp, pqn), S2);
-                dA[n] = fmaf(dt * gv[n], ahp, dA[n]);
-                red[n] = dt * uu * gv[n];                                  // dB contribution
-                red[NS + n] = dg * HS[((t + 1) * NS + n) * CHB + lane];    // dC contribution
-                carry[n] = fmaf(a, gv[n], dt * qtp);
-            }
-            // dP[n][k] += dt g_n qh_k ; dQ[k][n] += dt ptg_k hp_n   (this lane's channel)
-            for (int k = 0; k < r; ++k) {
+                for (int k = 0; k < RM; ++k) {
+                    pqn = fmaf(Pr[j][k], qh[k], pqn);
+                    qtp = fmaf(Qr[k][j], ptg[k], qtp);
+                }
+                const float ahp = a * hp[j], dtg = dt * gv[j];
+                S1 = fmaf(gv[j], bt[j], S1);
+                S2 = fmaf(gv[j], fmaf(An[j], ahp, pqn), S2);
+                dA[j] = fmaf(dtg, ahp, dA[j]);
+                red[j] = dtu * gv[j];        // dB contribution
+                red[SPT + j] = dg * hn[j];   // dC contribution
+                carry[j] = fmaf(a, gv[j], dt * qtp);
 #pragma unroll
-                for (int n = 0; n < NS; ++n) {
-                    dPm[(n * RM + k) * CHB + lane] = fmaf(dt * gv[n], qh[k], dPm[(n * RM + k) * CHB + lane]);
-                    dQm[(k * NS + n) * CHB + lane] = fmaf(dt * ptg[k], hp[n], dQm[(k * NS + n) * CHB + lane]);
+                for (int k = 0; k < RM; ++k) {
+                    dP[j][k] = fmaf(dtg, qh[k], dP[j][k]);
+                    dQ[k][j] = fmaf(dt * ptg[k], hp[j], dQ[k][j]);
                 }
             }
-            // sum dB / dC contributions over the warp's channels: lane j takes column j
-            __syncwarp();
-#pragma unroll
-            for (int j = 0; j < 2 * NS; ++j) RD[lane * 33 + j] = red[j];
-            __syncwarp();
+            S1 = quad_sum(S1);
+            S2 = quad_sum(S2);
+            if (qt == 0) {
+                const float uu = SU[t][ch];
+                const float ddt = fmaf(uu, S1, S2) * SGT[t][ch];
+                DU[t][ch] = fmaf(dt, S1, Dv * dg);
+                DD[t][ch] = ddt;
+                dDs = fmaf(dg, uu, dDs);
+                dbs += ddt;
+            }
+            // dB / dC: reduce-scatter the 8 values over the warp's 8 channels (lanes with
+            // this qt); afterwards lane (ch8 = lane >> 2, qt) holds value index ch8, summed
             {
-                float sacc = 0.f;
-#pragma unroll 8
-                for (int i = 0; i < 32; ++i) sacc += RD[i * 33 + lane];
-                const int n = lane & (NS - 1);
-                if (n < p.dstate) {
-                    float *dst = (lane < NS ? p.acc_dB : p.acc_dC) +
-                                 (((int64_t)b * p.n_groups + g) * p.dstate + n) * p.lpitch + t0 + t;
-                    atomicAdd(dst, sacc);
+                const bool b16 = (lane >> 4) & 1, b8 = (lane >> 3) & 1, b4 = (lane >> 2) & 1;
+                float w4[4], w2[2];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float send = b16 ? red[i] : red[4 + i], keep = b16 ? red[4 + i] : red[i];
+                    w4[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
                 }
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    const float send = b8 ? w4[i] : w4[2 + i], keep = b8 ? w4[2 + i] : w4[i];
+                    w2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+                }
+                const float send = b4 ? w2[0] : w2[1], keep = b4 ? w2[1] : w2[0];
+                WACC[wid][t][lane] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
             }
-            const float ddt = fmaf(uu, S1, S2) * SGT[t * CHB + lane];
-            const float du = fmaf(dt, S1, Dv * dg);
-            dDs = fmaf(dg, uu, dDs);
-            dbs += ddt;
-            SU[t * CHB + lane] = du;    // reuse: du and ddelta of step t
-            SDT[t * CHB + lane] = ddt;
         }
-        if (valid) {
+        __syncthreads();
+        // du / ddelta of the segment (the quad leader of each channel), dB / dC flush
+        if (qt == 0 && valid) {
             T *dur = reinterpret_cast<T *>(p.du) + (int64_t)b * p.du_bs + (int64_t)d * p.du_ds;
             T *ddr = reinterpret_cast<T *>(p.ddelta) + (int64_t)b * p.ddelta_bs + (int64_t)d * p.ddelta_ds;
 #pragma unroll
@@ -433,88 +429,111 @@ __global__ void __launch_bounds__(pq::CHB) ss_pq_bwd_kernel(const BwdParams p) {
                 float a1[8], a2[8];
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
-                    a1[j] = SU[(8 * hh + j) * CHB + lane];
-                    a2[j] = SDT[(8 * hh + j) * CHB + lane];
+                    a1[j] = DU[8 * hh + j][ch];
+                    a2[j] = DD[8 * hh + j][ch];
                 }
                 pq_store8(dur, t0 + 8 * hh, L, vec, a1);
                 pq_store8(ddr, t0 + 8 * hh, L, vec, a2);
             }
         }
-        __syncwarp();
+        {
+            // WACC slot (a lane index): qt = slot & 3, value index ch8 = slot >> 2: state
+            // 4 qt + (ch8 & 3), dB for ch8 < 4 and dC above
+            const int slot = tid >> 2, tq = tid & 3;
+            const int n = SPT * (slot & 3) + ((slot >> 2) & 3);
+            const bool isC = (slot >> 4) != 0;
+            float v[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float sum = 0.f;
+#pragma unroll
+                for (int ww = 0; ww < NW; ++ww) sum += WACC[ww][4 * tq + i][slot];
+                v[i] = sum;
+            }
+            if (n < p.dstate && 4 * tq < tv) {
+                float *dst = (isC ? p.acc_dC : p.acc_dB) + (((int64_t)b * p.n_groups + g) * p.dstate + n) * p.lpitch +
+                             t0 + 4 * tq;
+                if (4 * tq + 4 <= tv) {
+                    red_add_v4(dst, v[0], v[1], v[2], v[3]);
+                } else {
+                    for (int i = 0; i < 4; ++i)
+                        if (4 * tq + i < tv) atomicAdd(dst + i, v[i]);
+                }
+            }
+        }
     }
+    // per-channel sums
     if (valid) {
 #pragma unroll
-        for (int n = 0; n < NS; ++n)
-            if (n < p.dstate) atomicAdd(p.dA + (int64_t)d * p.dstate + n, dA[n]);
-        if (p.dD) atomicAdd(p.dD + d, dDs);
-        if (p.ddelta_bias) atomicAdd(p.ddelta_bias + d, dbs);
+        for (int j = 0; j < SPT; ++j) {
+            const int n = SPT * qt + j;
+            if (n < p.dstate) atomicAdd(p.dA + (int64_t)d * p.dstate + n, dA[j]);
+        }
+        if (qt == 0) {
+            if (p.dD) atomicAdd(p.dD + d, dDs);
+            if (p.ddelta_bias) atomicAdd(p.ddelta_bias + d, dbs);
+        }
     }
-    // dP / dQ: per channel, or summed over the warp's channels when shared
-    for (int idx = 0; idx < NS * RM; ++idx) {
-        const int n = idx / RM, k = idx - n * RM;
-        const int k2 = idx / NS, n2 = idx - k2 * NS;
-        float vp = valid ? dPm[idx * CHB + lane] : 0.f;
-        float vq = valid ? dQm[idx * CHB + lane] : 0.f;
-        if constexpr (PER_DIM) {
-            if (valid && n < p.dstate && k < r) atomicAdd(p.dP + ((int64_t)d * p.dstate + n) * r + k, vp);
-            if (valid && n2 < p.dstate && k2 < r) atomicAdd(p.dQ + ((int64_t)d * r + k2) * p.dstate + n2, vq);
-        } else {
+    // dP / dQ: per channel, or summed over the warp's 8 channels when shared
 #pragma unroll
-            for (int off = 16; off > 0; off >>= 1) {
-                vp += __shfl_xor_sync(0xffffffffu, vp, off);
-                vq += __shfl_xor_sync(0xffffffffu, vq, off);
-            }
-            if (lane == 0) {
-                if (n < p.dstate && k < r) atomicAdd(p.dP + n * r + k, vp);
-                if (n2 < p.dstate && k2 < r) atomicAdd(p.dQ + k2 * p.dstate + n2, vq);
+    for (int j = 0; j < SPT; ++j) {
+        const int n = SPT * qt + j;
+#pragma unroll
+        for (int k = 0; k < RM; ++k) {
+            float vp = valid ? dP[j][k] : 0.f, vq = valid ? dQ[k][j] : 0.f;
+            if (p.pq_per_dim) {
+                if (valid && n < p.dstate && k < r) {
+                    p.dP[((int64_t)d * p.dstate + n) * r + k] = vp;
+                    p.dQ[((int64_t)d * r + k) * p.dstate + n] = vq;
+                }
+            } else {
+#pragma unroll
+                for (int off = 4; off < 32; off <<= 1) {
+                    vp += __shfl_xor_sync(0xffffffffu, vp, off);
+                    vq += __shfl_xor_sync(0xffffffffu, vq, off);
+                }
+                if ((lane >> 2) == 0 && n < p.dstate && k < r) {
+                    atomicAdd(p.dP + n * r + k, vp);
+                    atomicAdd(p.dQ + k * p.dstate + n, vq);
+                }
             }
         }
     }
 }
 
-template <typename T, bool HAS_Z, bool PER_DIM>
+template <typename T, bool HAS_Z, int RM>
 static cudaError_t pq_fwd_t(FwdParams p, cudaStream_t st) {
-    constexpr int CH = pq::CHF, PW = PER_DIM ? CH : 1;
-    const int smem = (2 * pq::TT * pq::NS + 2 * pq::NS * pq::RM * PW) * 4;
-    auto kern = ss_pq_fwd_kernel<T, HAS_Z, PER_DIM>;
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e != cudaSuccess) return e;
-        configured = true;
-    }
-    p.tiles_per_group = (p.dpg + CH - 1) / CH;
+    p.tiles_per_group = (p.dpg + pq::CH - 1) / pq::CH;
     dim3 grid(p.tiles_per_group * p.n_groups, p.batch);
-    kern<<<grid, CH, smem, st>>>(p);
+    ss_pq_fwd_kernel<T, HAS_Z, RM><<<grid, pq::NT, 0, st>>>(p);
     return cudaGetLastError();
 }
 
-template <typename T, bool HAS_Z, bool PER_DIM>
+template <typename T, bool HAS_Z, int RM>
 static cudaError_t pq_bwd_t(BwdParams p, cudaStream_t st) {
-    using Ly = PqBwdLayout<T, HAS_Z, PER_DIM>;
-    const int smem = Ly::FLOATS * 4;
-    auto kern = ss_pq_bwd_kernel<T, HAS_Z, PER_DIM>;
+    auto kern = ss_pq_bwd_kernel<T, HAS_Z, RM>;
+    constexpr int SMEM = (int)sizeof(PqBwdSmem);
     static bool configured = false;
     if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
         if (e != cudaSuccess) return e;
         configured = true;
     }
-    p.tiles_per_group = (p.dpg + pq::CHB - 1) / pq::CHB;
+    p.tiles_per_group = (p.dpg + pq::CH - 1) / pq::CH;
     dim3 grid(p.tiles_per_group * p.n_groups, p.batch);
-    kern<<<grid, pq::CHB, smem, st>>>(p);
+    kern<<<grid, pq::NT, SMEM, st>>>(p);
     return cudaGetLastError();
 }
 
 template <typename T>
 static cudaError_t pq_fwd_dispatch(const FwdParams &p, bool has_z, cudaStream_t st) {
-    if (p.pq_per_dim) return has_z ? pq_fwd_t<T, true, true>(p, st) : pq_fwd_t<T, false, true>(p, st);
-    return has_z ? pq_fwd_t<T, true, false>(p, st) : pq_fwd_t<T, false, false>(p, st);
+    if (p.pq_rank <= 4) return has_z ? pq_fwd_t<T, true, 4>(p, st) : pq_fwd_t<T, false, 4>(p, st);
+    return has_z ? pq_fwd_t<T, true, 8>(p, st) : pq_fwd_t<T, false, 8>(p, st);
 }
 template <typename T>
 static cudaError_t pq_bwd_dispatch(const BwdParams &p, bool has_z, cudaStream_t st) {
-    if (p.pq_per_dim) return has_z ? pq_bwd_t<T, true, true>(p, st) : pq_bwd_t<T, false, true>(p, st);
-    return has_z ? pq_bwd_t<T, true, false>(p, st) : pq_bwd_t<T, false, false>(p, st);
+    if (p.pq_rank <= 4) return has_z ? pq_bwd_t<T, true, 4>(p, st) : pq_bwd_t<T, false, 4>(p, st);
+    return has_z ? pq_bwd_t<T, true, 8>(p, st) : pq_bwd_t<T, false, 8>(p, st);
 }
 
 cudaError_t launch_ss_fwd_pq(const FwdParams &p, int itype, bool has_z, cudaStream_t st) {
