@@ -78,7 +78,7 @@ typedef struct {
     void *workspace;    int64_t workspace_bytes;
     /* motif low-rank coupling h += dt * P (Q h_prev) (selective_scan_interface.py:402-433);
      * P == NULL disables it.  fp32 contiguous: P (dstate, r) and Q (r, dstate), or per channel
-     * P (dim, dstate, r) and Q (dim, r, dstate) when pq_per_dim; r = pq_rank <= 8, dstate <= 16. */
+     * P (dim, dstate, r) and Q (dim, r, dstate) when pq_per_dim; r = pq_rank <= 8, dstate <= 64. */
     const float *P;     const float *Q;
     int64_t pq_rank;    int32_t pq_per_dim; int32_t _pad_pq;
 } ss_fwd_args;

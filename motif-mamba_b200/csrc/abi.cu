@@ -61,12 +61,12 @@ FwdShape fwd_shape(const ss_fwd_args *a) {
     return s;
 }
 
-// Motif coupling limits: P and Q both given, rank 1..8, dstate <= 16 (states in registers).
+// Motif coupling limits: P and Q both given, rank 1..8, dstate <= 64 (4 states per lane).
 int check_pq(const char *who, const float *P, const float *Q, int64_t rank, int64_t dstate) {
     if (!P && !Q) return MSS_OK;
     if (!P || !Q) return fail(MSS_ERR_INVALID, "%s: P and Q must be given together", who);
     if (rank < 1 || rank > 8) return fail(MSS_ERR_UNSUPPORTED, "%s: pq_rank must be in [1, 8]", who);
-    if (dstate > 16) return fail(MSS_ERR_UNSUPPORTED, "%s: the P/Q coupling supports dstate <= 16", who);
+    if (dstate > 64) return fail(MSS_ERR_UNSUPPORTED, "%s: the P/Q coupling supports dstate <= 64", who);
     return MSS_OK;
 }
 
@@ -135,7 +135,8 @@ BwdShape bwd_shape(const ss_bwd_args *a) {
     // dstate > 16: fp32 per-step partial sums over states, carried between state blocks
     s.dh_bytes = a->dstate > 16 ? round_up(rows * 2 * s.lpitch * 4, 256) : 0;
     // P/Q coupling: the 16 states at every 16-step segment start
-    s.ckpt_bytes = a->P ? round_up(rows * ((a->seqlen + 15) / 16) * 16 * 4, 256) : 0;
+    const int64_t nsx = a->dstate <= 16 ? 16 : (a->dstate <= 32 ? 32 : 64);  // padded states per checkpoint
+    s.ckpt_bytes = a->P ? round_up(rows * ((a->seqlen + 15) / 16) * nsx * 4, 256) : 0;
     return s;
 }
 

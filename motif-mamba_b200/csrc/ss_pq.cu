@@ -4,24 +4,23 @@
 //
 // (reference: selective_scan_ref with P/Q, mamba_ssm/ops/selective_scan_interface.py:402-433;
 // full-matrix path :262-350).  P is (dstate, r) shared or (dim, dstate, r) per channel, Q is
-// (r, dstate) or (dim, r, dstate), r <= 8, dstate <= 16.  The coupling mixes states, so the
+// (r, dstate) or (dim, r, dstate), r <= 8, dstate <= 64.  The coupling mixes states, so the
 // diagonal-scan tricks of ss_fwd / ss_bwd do not apply and time stays sequential per channel.
-// To give the GPU enough warps, a channel's 16 states are split over a quad of 4 adjacent
-// lanes (4 states each): per step q = Q h is a quad sum (two shuffles per rank), pq = P q,
-// the diagonal update and the output's quad sum.  Each lane keeps its slice of P and Q in
+// To give the GPU enough warps, a channel's states (padded to 16, 32 or 64) are split over
+// 4, 8 or 16 adjacent lanes, 4 states each: per step q = Q h is a sum over those lanes
+// (shuffles), pq = P q, the diagonal update and the output's sum.  Each lane keeps its slice of P and Q in
 // registers (rows n of P, columns n of Q for its 4 states), and in the backward also its
 // slice of dP and dQ, so nothing is accumulated through shared memory per step.
 //
-// Forward: B/C tiles of 32 steps are staged in shared memory for the CTA's 32 channels;
-// u/delta/z rows are read by the channel's quad with 16-byte loads; x gets the state every
+// Forward: B/C tiles of 32 steps are staged in shared memory for the CTA's channels;
+// u/delta/z rows are read by the channel's lanes with 16-byte loads; x gets the state every
 // 256 steps as in ss_fwd.
 // Backward (O(L)): a forward sweep stores the state at every 16-step segment start in a
 // workspace; then segments are processed in reverse: the 16 states of each step are
 // recomputed into shared memory and the adjoint g_t = C_t doutg_t + M_{t+1}^T g_{t+1}
 // (M = diag(a) + dt P Q, M^T g = a g + dt Q^T (P^T g)) runs backwards, accumulating du,
 // ddelta, dA, dD, ddelta_bias, dP = sum dt g (Q h_prev)^T and dQ = sum dt (P^T g) h_prev^T.
-// dB / dC (sums over channels) are reduce-scattered over the warp's 8 channels with
-// shuffles, summed over the CTA's 4 warps per segment in shared memory, and added to the
+// dB / dC (sums over channels) are reduce-scattered over the warp's channels with shuffles, summed over the CTA's 4 warps per segment in shared memory, and added to the
 // fp32 accumulators with one vector atomic per thread and segment.
 #include "common.cuh"
 #include "kernels.h"
@@ -29,12 +28,17 @@
 namespace mss {
 
 namespace pq {
-constexpr int NS = 16;   // states (dstate <= 16, zero padded)
-constexpr int SPT = 4;   // states per lane (a quad of lanes per channel)
-constexpr int NT = 128;  // threads per CTA = 32 channels
-constexpr int CH = NT / 4;
+constexpr int SPT = 4;   // states per lane
+constexpr int NT = 128;  // threads per CTA
 constexpr int TT = 32;   // forward tile (divides the 256-step x chunk)
 constexpr int SEG = 16;  // backward segment length
+// A channel's NSX states (dstate padded to 16, 32 or 64) sit on LPC = NSX / 4 adjacent lanes.
+template <int NSX> struct Geo {
+    static constexpr int LPC = NSX / SPT;      // lanes per channel
+    static constexpr int CH = NT / LPC;        // channels per CTA
+    static constexpr int CPW = 32 / LPC;       // channels per warp
+    static constexpr int VPL = 8 / CPW;        // dB / dC values a lane keeps after the warp reduction
+};
 }  // namespace pq
 
 template <typename T>
@@ -56,9 +60,11 @@ __device__ __forceinline__ void pq_store8(T *row, int64_t t0, int64_t L, bool ve
             if (t0 + i < L) row[t0 + i] = from_f<T>(v[i]);
     }
 }
-__device__ __forceinline__ float quad_sum(float v) {
-    v += __shfl_xor_sync(0xffffffffu, v, 1);
-    return v + __shfl_xor_sync(0xffffffffu, v, 2);
+// Sum over the LPC lanes of a channel.
+template <int LPC> __device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+    for (int off = 1; off < LPC; off <<= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    return v;
 }
 
 // This lane's slice of P (rows n = 4 qt + j) and Q (columns n), zero beyond dstate / r.
@@ -81,7 +87,7 @@ __device__ __forceinline__ void load_pq_slice(const float *P, const float *Q, bo
 }
 
 // One step of the coupled recurrence for this lane's 4 states (h holds h_{t-1} on entry).
-template <int RM>
+template <int RM, int LPC>
 __device__ __forceinline__ void pq_step(float (&h)[pq::SPT], const float (&Pr)[pq::SPT][RM],
                                         const float (&Qr)[RM][pq::SPT], const float (&A2)[pq::SPT], float dt,
                                         float dtu, const float *bt) {
@@ -91,7 +97,7 @@ __device__ __forceinline__ void pq_step(float (&h)[pq::SPT], const float (&Pr)[p
         float s = 0.f;
 #pragma unroll
         for (int j = 0; j < pq::SPT; ++j) s = fmaf(Qr[k][j], h[j], s);
-        q[k] = quad_sum(s);
+        q[k] = group_sum<LPC>(s);
     }
 #pragma unroll
     for (int j = 0; j < pq::SPT; ++j) {
@@ -102,11 +108,12 @@ __device__ __forceinline__ void pq_step(float (&h)[pq::SPT], const float (&Pr)[p
     }
 }
 
-template <typename T, bool HAS_Z, int RM>
+template <typename T, bool HAS_Z, int RM, int NSX>
 __global__ void __launch_bounds__(pq::NT) ss_pq_fwd_kernel(const FwdParams p) {
     using namespace pq;
+    constexpr int NS = NSX, LPC = Geo<NSX>::LPC, CH = Geo<NSX>::CH;
     __shared__ __align__(16) float Bs[TT][NS], Cs[TT][NS];
-    const int tid = threadIdx.x, ch = tid >> 2, qt = tid & 3;
+    const int tid = threadIdx.x, ch = tid / LPC, qt = tid % LPC;
     const int g = blockIdx.x / p.tiles_per_group, tile = blockIdx.x - g * p.tiles_per_group;
     const int b = blockIdx.y;
     const int cin = tile * CH + ch;
@@ -157,11 +164,11 @@ __global__ void __launch_bounds__(pq::NT) ss_pq_fwd_kernel(const FwdParams p) {
                 dt = (valid && tg + j < L) ? dt : 0.f;
                 cum += dt;
                 const float *bt = &Bs[g8 + j][SPT * qt], *ct = &Cs[g8 + j][SPT * qt];
-                pq_step<RM>(h, Pr, Qr, A2, dt, dt * uf[j], bt);
+                pq_step<RM, LPC>(h, Pr, Qr, A2, dt, dt * uf[j], bt);
                 float yp = 0.f;
 #pragma unroll
                 for (int k = 0; k < SPT; ++k) yp = fmaf(ct[k], h[k], yp);
-                y[j] = fmaf(Dv, uf[j], quad_sum(yp));
+                y[j] = fmaf(Dv, uf[j], group_sum<LPC>(yp));
             }
             if (valid && qt == 0) {
                 pq_store8(orow, tg, L, vec, y);
@@ -189,20 +196,32 @@ __global__ void __launch_bounds__(pq::NT) ss_pq_fwd_kernel(const FwdParams p) {
     }
 }
 
-struct PqBwdSmem {
-    float HS[pq::SEG + 1][pq::NT][pq::SPT];  // states of the segment, per lane
-    float Bs[pq::SEG][pq::NS], Cs[pq::SEG][pq::NS];
-    float SV[5][pq::SEG][pq::CH];            // per channel and step: u, dt, dt u, doutg, gate
-    float DU[pq::SEG][pq::CH], DD[pq::SEG][pq::CH];
-    float WACC[pq::NT / 32][pq::SEG][32];    // warp sums of dB / dC per step
+template <int NSX> struct PqBwdSmem {
+    using G = pq::Geo<NSX>;
+    float HS[pq::SEG + 1][pq::NT][pq::SPT];      // states of the segment, per lane
+    float Bs[pq::SEG][NSX], Cs[pq::SEG][NSX];
+    float SV[5][pq::SEG][G::CH];                 // per channel and step: u, dt, dt u, doutg, gate
+    float DU[pq::SEG][G::CH], DD[pq::SEG][G::CH];
+    float WACC[pq::NT / 32][pq::SEG][32][G::VPL];  // warp sums of dB / dC per step
 };
 
-template <typename T, bool HAS_Z, int RM>
+// After the warp's reduce-scatter over channels, lane `ln` keeps the dB / dC values
+// [base, base + VPL) of its channel-group slot: halving on lane bits 16, 8, 4 (those above
+// the LPC lanes of a channel), the set bit keeping the upper half.
+template <int LPC> __device__ __forceinline__ int rs_base(int ln) {
+    int base = 0;
+#pragma unroll
+    for (int m = 16, half = 4; m >= LPC; m >>= 1, half >>= 1)
+        if (ln & m) base += half;
+    return base;
+}
+
+template <typename T, bool HAS_Z, int RM, int NSX>
 __global__ void __launch_bounds__(pq::NT) ss_pq_bwd_kernel(const BwdParams p) {
     using namespace pq;
-    constexpr int NW = NT / 32;
+    constexpr int NW = NT / 32, NS = NSX, LPC = Geo<NSX>::LPC, CH = Geo<NSX>::CH, VPL = Geo<NSX>::VPL;
     extern __shared__ __align__(16) char pq_smem[];
-    PqBwdSmem &S = *reinterpret_cast<PqBwdSmem *>(pq_smem);
+    PqBwdSmem<NSX> &S = *reinterpret_cast<PqBwdSmem<NSX> *>(pq_smem);
     auto &HS = S.HS;
     auto &Bs = S.Bs;
     auto &Cs = S.Cs;
@@ -215,7 +234,7 @@ __global__ void __launch_bounds__(pq::NT) ss_pq_bwd_kernel(const BwdParams p) {
     float(&SDTU)[SEG][CH] = SV[2];
     float(&SDG)[SEG][CH] = SV[3];
     float(&SGT)[SEG][CH] = SV[4];
-    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, ch = tid >> 2, qt = tid & 3;
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, ch = tid / LPC, qt = tid % LPC;
     const int g = blockIdx.x / p.tiles_per_group, tile = blockIdx.x - g * p.tiles_per_group;
     const int b = blockIdx.y;
     const int cin = tile * CH + ch;
@@ -317,7 +336,7 @@ __global__ void __launch_bounds__(pq::NT) ss_pq_bwd_kernel(const BwdParams p) {
             __syncthreads();
             const int tv = (int)min((int64_t)SEG, L - t0);
             for (int t = 0; t < tv; ++t)
-                pq_step<RM>(h, Pr, Qr, A2, SDT[t][ch], SDTU[t][ch], &Bs[t][SPT * qt]);
+                pq_step<RM, LPC>(h, Pr, Qr, A2, SDT[t][ch], SDTU[t][ch], &Bs[t][SPT * qt]);
         }
     }
 
@@ -342,7 +361,7 @@ __global__ void __launch_bounds__(pq::NT) ss_pq_bwd_kernel(const BwdParams p) {
             float h[SPT] = {c4.x, c4.y, c4.z, c4.w};
             *reinterpret_cast<float4 *>(&HS[0][tid][0]) = c4;
             for (int t = 0; t < tv; ++t) {
-                pq_step<RM>(h, Pr, Qr, A2, SDT[t][ch], SDTU[t][ch], &Bs[t][SPT * qt]);
+                pq_step<RM, LPC>(h, Pr, Qr, A2, SDT[t][ch], SDTU[t][ch], &Bs[t][SPT * qt]);
                 *reinterpret_cast<float4 *>(&HS[t + 1][tid][0]) = make_float4(h[0], h[1], h[2], h[3]);
             }
         }
@@ -364,8 +383,8 @@ __global__ void __launch_bounds__(pq::NT) ss_pq_bwd_kernel(const BwdParams p) {
                     s1 = fmaf(Qr[k][j], hp[j], s1);
                     s2 = fmaf(Pr[j][k], gv[j], s2);
                 }
-                qh[k] = quad_sum(s1);
-                ptg[k] = quad_sum(s2);
+                qh[k] = group_sum<LPC>(s1);
+                ptg[k] = group_sum<LPC>(s2);
             }
             float S1 = 0.f, S2 = 0.f, red[2 * SPT];
 #pragma unroll
@@ -390,8 +409,8 @@ __global__ void __launch_bounds__(pq::NT) ss_pq_bwd_kernel(const BwdParams p) {
                     dQ[k][j] = fmaf(dt * ptg[k], hp[j], dQ[k][j]);
                 }
             }
-            S1 = quad_sum(S1);
-            S2 = quad_sum(S2);
+            S1 = group_sum<LPC>(S1);
+            S2 = group_sum<LPC>(S2);
             if (qt == 0) {
                 const float uu = SU[t][ch];
                 const float ddt = fmaf(uu, S1, S2) * SGT[t][ch];
@@ -400,23 +419,20 @@ __global__ void __launch_bounds__(pq::NT) ss_pq_bwd_kernel(const BwdParams p) {
                 dDs = fmaf(dg, uu, dDs);
                 dbs += ddt;
             }
-            // dB / dC: reduce-scatter the 8 values over the warp's 8 channels (lanes with
-            // this qt); afterwards lane (ch8 = lane >> 2, qt) holds value index ch8, summed
+            // dB / dC: reduce-scatter the 8 values over the warp's channels (lanes with this
+            // qt): after it the lane keeps values [rs_base(lane), + VPL), summed
             {
-                const bool b16 = (lane >> 4) & 1, b8 = (lane >> 3) & 1, b4 = (lane >> 2) & 1;
-                float w4[4], w2[2];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float send = b16 ? red[i] : red[4 + i], keep = b16 ? red[4 + i] : red[i];
-                    w4[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+                for (int m = 16, half = 4; m >= LPC; m >>= 1, half >>= 1) {
+                    const bool up = (lane & m) != 0;
+#pragma unroll
+                    for (int i = 0; i < half; ++i) {
+                        const float send = up ? red[i] : red[half + i], keep = up ? red[half + i] : red[i];
+                        red[i] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+                    }
                 }
 #pragma unroll
-                for (int i = 0; i < 2; ++i) {
-                    const float send = b8 ? w4[i] : w4[2 + i], keep = b8 ? w4[2 + i] : w4[i];
-                    w2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-                }
-                const float send = b4 ? w2[0] : w2[1], keep = b4 ? w2[1] : w2[0];
-                WACC[wid][t][lane] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+                for (int i = 0; i < VPL; ++i) WACC[wid][t][lane][i] = red[i];
             }
         }
         __syncthreads();
@@ -436,18 +452,19 @@ __global__ void __launch_bounds__(pq::NT) ss_pq_bwd_kernel(const BwdParams p) {
                 pq_store8(ddr, t0 + 8 * hh, L, vec, a2);
             }
         }
-        {
-            // WACC slot (a lane index): qt = slot & 3, value index ch8 = slot >> 2: state
-            // 4 qt + (ch8 & 3), dB for ch8 < 4 and dC above
-            const int slot = tid >> 2, tq = tid & 3;
-            const int n = SPT * (slot & 3) + ((slot >> 2) & 3);
-            const bool isC = (slot >> 4) != 0;
+        // WACC entry (lane ln, value i): state SPT * (ln % LPC) + (idx & 3) with idx =
+        // rs_base(ln) + i, dB for idx < 4 and dC above; 4 steps per item, one vector atomic each
+        for (int it = tid; it < 32 * VPL * 4; it += NT) {
+            const int sv = it >> 2, tq = it & 3, ln = sv / VPL, vi = sv - ln * VPL;
+            const int idx = rs_base<LPC>(ln) + vi;
+            const int n = SPT * (ln % LPC) + (idx & 3);
+            const bool isC = idx >= 4;
             float v[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 float sum = 0.f;
 #pragma unroll
-                for (int ww = 0; ww < NW; ++ww) sum += WACC[ww][4 * tq + i][slot];
+                for (int ww = 0; ww < NW; ++ww) sum += WACC[ww][4 * tq + i][ln][vi];
                 v[i] = sum;
             }
             if (n < p.dstate && 4 * tq < tv) {
@@ -474,25 +491,25 @@ __global__ void __launch_bounds__(pq::NT) ss_pq_bwd_kernel(const BwdParams p) {
             if (p.ddelta_bias) atomicAdd(p.ddelta_bias + d, dbs);
         }
     }
-    // dP / dQ: per channel, or summed over the warp's 8 channels when shared
+    // dP / dQ: per channel, or summed over the warp's channels when shared (and over the batch)
 #pragma unroll
     for (int j = 0; j < SPT; ++j) {
         const int n = SPT * qt + j;
 #pragma unroll
         for (int k = 0; k < RM; ++k) {
             float vp = valid ? dP[j][k] : 0.f, vq = valid ? dQ[k][j] : 0.f;
-            if (p.pq_per_dim) {
+            if (p.pq_per_dim) {  // summed over the batch rows (one CTA row each)
                 if (valid && n < p.dstate && k < r) {
-                    p.dP[((int64_t)d * p.dstate + n) * r + k] = vp;
-                    p.dQ[((int64_t)d * r + k) * p.dstate + n] = vq;
+                    atomicAdd(p.dP + ((int64_t)d * p.dstate + n) * r + k, vp);
+                    atomicAdd(p.dQ + ((int64_t)d * r + k) * p.dstate + n, vq);
                 }
             } else {
 #pragma unroll
-                for (int off = 4; off < 32; off <<= 1) {
+                for (int off = LPC; off < 32; off <<= 1) {
                     vp += __shfl_xor_sync(0xffffffffu, vp, off);
                     vq += __shfl_xor_sync(0xffffffffu, vq, off);
                 }
-                if ((lane >> 2) == 0 && n < p.dstate && k < r) {
+                if (lane < LPC && n < p.dstate && k < r) {
                     atomicAdd(p.dP + n * r + k, vp);
                     atomicAdd(p.dQ + k * p.dstate + n, vq);
                 }
@@ -501,39 +518,53 @@ __global__ void __launch_bounds__(pq::NT) ss_pq_bwd_kernel(const BwdParams p) {
     }
 }
 
-template <typename T, bool HAS_Z, int RM>
+template <typename T, bool HAS_Z, int RM, int NSX>
 static cudaError_t pq_fwd_t(FwdParams p, cudaStream_t st) {
-    p.tiles_per_group = (p.dpg + pq::CH - 1) / pq::CH;
+    constexpr int CH = pq::Geo<NSX>::CH;
+    p.tiles_per_group = (p.dpg + CH - 1) / CH;
     dim3 grid(p.tiles_per_group * p.n_groups, p.batch);
-    ss_pq_fwd_kernel<T, HAS_Z, RM><<<grid, pq::NT, 0, st>>>(p);
+    ss_pq_fwd_kernel<T, HAS_Z, RM, NSX><<<grid, pq::NT, 0, st>>>(p);
     return cudaGetLastError();
 }
 
-template <typename T, bool HAS_Z, int RM>
+template <typename T, bool HAS_Z, int RM, int NSX>
 static cudaError_t pq_bwd_t(BwdParams p, cudaStream_t st) {
-    auto kern = ss_pq_bwd_kernel<T, HAS_Z, RM>;
-    constexpr int SMEM = (int)sizeof(PqBwdSmem);
+    auto kern = ss_pq_bwd_kernel<T, HAS_Z, RM, NSX>;
+    constexpr int SMEM = (int)sizeof(PqBwdSmem<NSX>);
+    constexpr int CH = pq::Geo<NSX>::CH;
     static bool configured = false;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
         if (e != cudaSuccess) return e;
         configured = true;
     }
-    p.tiles_per_group = (p.dpg + pq::CH - 1) / pq::CH;
+    p.tiles_per_group = (p.dpg + CH - 1) / CH;
     dim3 grid(p.tiles_per_group * p.n_groups, p.batch);
     kern<<<grid, pq::NT, SMEM, st>>>(p);
     return cudaGetLastError();
 }
 
+template <typename T, int NSX>
+static cudaError_t pq_fwd_ns(const FwdParams &p, bool has_z, cudaStream_t st) {
+    if (p.pq_rank <= 4) return has_z ? pq_fwd_t<T, true, 4, NSX>(p, st) : pq_fwd_t<T, false, 4, NSX>(p, st);
+    return has_z ? pq_fwd_t<T, true, 8, NSX>(p, st) : pq_fwd_t<T, false, 8, NSX>(p, st);
+}
+template <typename T, int NSX>
+static cudaError_t pq_bwd_ns(const BwdParams &p, bool has_z, cudaStream_t st) {
+    if (p.pq_rank <= 4) return has_z ? pq_bwd_t<T, true, 4, NSX>(p, st) : pq_bwd_t<T, false, 4, NSX>(p, st);
+    return has_z ? pq_bwd_t<T, true, 8, NSX>(p, st) : pq_bwd_t<T, false, 8, NSX>(p, st);
+}
 template <typename T>
 static cudaError_t pq_fwd_dispatch(const FwdParams &p, bool has_z, cudaStream_t st) {
-    if (p.pq_rank <= 4) return has_z ? pq_fwd_t<T, true, 4>(p, st) : pq_fwd_t<T, false, 4>(p, st);
-    return has_z ? pq_fwd_t<T, true, 8>(p, st) : pq_fwd_t<T, false, 8>(p, st);
+    if (p.dstate <= 16) return pq_fwd_ns<T, 16>(p, has_z, st);
+    if (p.dstate <= 32) return pq_fwd_ns<T, 32>(p, has_z, st);
+    return pq_fwd_ns<T, 64>(p, has_z, st);
 }
 template <typename T>
 static cudaError_t pq_bwd_dispatch(const BwdParams &p, bool has_z, cudaStream_t st) {
-    if (p.pq_rank <= 4) return has_z ? pq_bwd_t<T, true, 4>(p, st) : pq_bwd_t<T, false, 4>(p, st);
-    return has_z ? pq_bwd_t<T, true, 8>(p, st) : pq_bwd_t<T, false, 8>(p, st);
+    if (p.dstate <= 16) return pq_bwd_ns<T, 16>(p, has_z, st);
+    if (p.dstate <= 32) return pq_bwd_ns<T, 32>(p, has_z, st);
+    return pq_bwd_ns<T, 64>(p, has_z, st);
 }
 
 cudaError_t launch_ss_fwd_pq(const FwdParams &p, int itype, bool has_z, cudaStream_t st) {

@@ -8,7 +8,7 @@ allocates) and the work runs in ``libmotif_ssm.so`` on the current CUDA stream.
 Differences from the reference, all raising instead of silently diverging:
 * complex ``A`` and constant (2-D) ``B`` / ``C`` raise ``NotImplementedError``;
 * ``P`` / ``Q`` (the motif low-rank coupling, ``:342-369``) must be contiguous fp32 with
-  ``dstate <= 16`` (the reference allows 256); ``gamma`` is checked and, as in the
+  ``dstate <= 64`` (the reference allows 256); ``gamma`` is checked and, as in the
   reference's dense P/Q kernels, not used;
 * ``dstate`` above ``MAX_DSTATE`` (64) raises (the reference allows 256);
 * ``x`` holds one (decay, state) pair per ``CHUNK_LEN`` = 256 steps instead of 2048;
@@ -67,8 +67,8 @@ def _check_pq(P, Q, gamma, dim, dstate):
         _req(P.size(-1) <= 8, "Current dense CUDA forward supports pq_rank <= 8")
         _req(P.dtype == torch.float32 and Q.dtype == torch.float32, "P and Q must be float32")
         _req(P.is_contiguous() and Q.is_contiguous(), "P and Q must be contiguous")
-        if dstate > 16:
-            raise NotImplementedError("selective_scan_cuda: the P/Q coupling supports dstate <= 16 in this library")
+        if dstate > 64:
+            raise NotImplementedError("selective_scan_cuda: the P/Q coupling supports dstate <= 64 in this library")
     if gamma is not None:
         _req(gamma.is_cuda, "gamma must be CUDA tensor")
         _req(gamma.dim() in (1, 2), "gamma must be 1D or 2D")
