@@ -1,12 +1,13 @@
 // Device-side helpers shared by the selective-scan, conv1d and state-update kernels.
 // sm_100a only.  Element types: float, __half, __nv_bfloat16.
 #pragma once
-#include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_runtime.h>
 #include <stdint.h>
 
 #include <algorithm>
+#include <atomic>
 
 #include "motif_ssm.h"
 
@@ -240,6 +241,19 @@ __device__ __forceinline__ void store_tile(T *g0, int64_t rstride, const char *s
                 g0[(int64_t)r * rstride + t0 + tt] = *reinterpret_cast<const T *>(ssrc + r * rp + tt * (int)sizeof(T));
         }
     }
+}
+
+// Raises a kernel's dynamic shared-memory limit once per device (the attribute is per device
+// context); `mask` is the call site's record of the devices already done.
+inline cudaError_t set_smem_once(std::atomic<unsigned long long> &mask, const void *fn, int bytes) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const unsigned long long bit = 1ull << (dev & 63);
+    if (mask.load(std::memory_order_acquire) & bit) return cudaSuccess;
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) mask.fetch_or(bit, std::memory_order_acq_rel);
+    return e;
 }
 
 }  // namespace mss

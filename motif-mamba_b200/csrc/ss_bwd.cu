@@ -612,11 +612,10 @@ template <typename T, bool HAS_Z>
 static cudaError_t launch_bwd_t(const BwdParams &p, cudaStream_t st) {
     auto kern = ss_bwd_kernel<T, HAS_Z>;
     constexpr int SMEM = (int)sizeof(BwdSmemT<T>);
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    static std::atomic<unsigned long long> smem_set{0};
+    {
+        const cudaError_t e = set_smem_once(smem_set, reinterpret_cast<const void *>(kern), SMEM);
         if (e != cudaSuccess) return e;
-        configured = true;
     }
     dim3 grid(p.tiles_per_group * p.n_groups, p.batch);
     kern<<<grid, bwd::NT, SMEM, st>>>(p);

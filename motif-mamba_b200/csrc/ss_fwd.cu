@@ -254,11 +254,10 @@ template <typename T, int NS, bool HAS_Z, bool CARRY>
 static cudaError_t launch_one(const FwdParams &p, dim3 grid, cudaStream_t st) {
     using Ly = FwdLayout<T, NS, HAS_Z, CARRY>;
     auto kern = ss_fwd_kernel<T, NS, HAS_Z, CARRY>;
-    static bool configured = false;  // idempotent attribute set; racing threads set the same value
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Ly::SMEM);
+    static std::atomic<unsigned long long> smem_set{0};
+    {
+        const cudaError_t e = set_smem_once(smem_set, reinterpret_cast<const void *>(kern), Ly::SMEM);
         if (e != cudaSuccess) return e;
-        configured = true;
     }
     kern<<<grid, Ly::CH, Ly::SMEM, st>>>(p);
     return cudaGetLastError();

@@ -532,11 +532,10 @@ static cudaError_t pq_bwd_t(BwdParams p, cudaStream_t st) {
     auto kern = ss_pq_bwd_kernel<T, HAS_Z, RM, NSX>;
     constexpr int SMEM = (int)sizeof(PqBwdSmem<NSX>);
     constexpr int CH = pq::Geo<NSX>::CH;
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    static std::atomic<unsigned long long> smem_set{0};
+    {
+        const cudaError_t e = set_smem_once(smem_set, reinterpret_cast<const void *>(kern), SMEM);
         if (e != cudaSuccess) return e;
-        configured = true;
     }
     p.tiles_per_group = (p.dpg + CH - 1) / CH;
     dim3 grid(p.tiles_per_group * p.n_groups, p.batch);
