@@ -162,6 +162,26 @@ typedef struct {
     void *out;          int64_t out_bs;
 } ssm_state_update_args;
 
+/* Residual add + RMSNorm of the pre-norm stack (the fused Add -> Norm the reference runs with
+ * fused_add_norm and residual_in_fp32, mamba_ssm/models/mixer_seq_simple.py:190-211):
+ * residual_out = x + residual_in (residual_in NULL: x), out = residual_out * rsqrt(mean(
+ * residual_out^2) + eps) * weight, computed in fp32 from residual_out as stored.  Rows of
+ * `dim` elements (dim % 8 == 0, <= 2048) with unit stride and 16-byte-aligned row starts. */
+typedef struct {
+    int64_t rows, dim;
+    int32_t itype;      /* x and out */
+    int32_t rin_type;   /* residual_in: MSS_F32 or itype */
+    int32_t rout_type;  /* residual_out: MSS_F32 or itype */
+    int32_t wtype;      /* weight: MSS_F32 or itype */
+    const void *x;              int64_t x_rs;
+    const void *residual_in;    int64_t rin_rs;        /* nullable */
+    void *residual_out;         int64_t rout_rs;
+    const void *weight;
+    void *out;                  int64_t out_rs;
+    float *rstd;                                       /* nullable (rows,): 1 / rms per row */
+    float eps;                  int32_t _pad;
+} add_rms_norm_args;
+
 /* Workspace bytes ss_fwd / ss_bwd need for these arguments (0 means none). */
 MSS_API int ss_fwd_workspace_size(const ss_fwd_args *a, int64_t *bytes);
 MSS_API int ss_bwd_workspace_size(const ss_bwd_args *a, int64_t *bytes);
@@ -192,6 +212,12 @@ MSS_API int conv1d_bwd(const conv1d_args *a, void *stream);
 MSS_API int conv1d_update(const conv1d_update_args *a, void *stream);
 /* one decode step of the SSM: updates state in place, writes out */
 MSS_API int ssm_state_update(const ssm_state_update_args *a, void *stream);
+
+/* Residual add + RMSNorm above (replaces the reference's fused layer_norm_fn(prenorm=True) call,
+ * mamba_ssm/models/mixer_seq_simple.py:190-211, whose Triton source the export lacks). */
+MSS_API int add_rms_norm(const add_rms_norm_args *a, void *stream);
+/* sizeof(add_rms_norm_args), for binding-side layout checks. */
+MSS_API int64_t add_rms_norm_args_size(void);
 
 /* Message of the last failure on the calling thread ("" if none). */
 MSS_API const char *ss_last_error(void);

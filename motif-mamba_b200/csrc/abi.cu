@@ -385,4 +385,26 @@ int ssm_state_update(const ssm_state_update_args *a, void *stream) {
     return e == cudaSuccess ? MSS_OK : cuda_fail(e, "ssm_state_update launch");
 }
 
+int64_t add_rms_norm_args_size(void) { return (int64_t)sizeof(add_rms_norm_args); }
+
+int add_rms_norm(const add_rms_norm_args *a, void *stream) {
+    if (!a) return fail(MSS_ERR_INVALID, "add_rms_norm: null argument struct");
+    if (!valid_type(a->itype)) return fail(MSS_ERR_INVALID, "add_rms_norm: bad element type");
+    for (int t : {a->rin_type, a->rout_type, a->wtype})
+        if (t != MSS_F32 && t != a->itype) return fail(MSS_ERR_INVALID, "add_rms_norm: residual / weight type must be f32 or itype");
+    if (a->rows < 0 || a->dim < 0) return fail(MSS_ERR_INVALID, "add_rms_norm: negative size");
+    if (a->dim % 8 != 0 || a->dim > 2048)
+        return fail(MSS_ERR_UNSUPPORTED, "add_rms_norm: dim must be a multiple of 8 and at most 2048");
+    if (a->rows == 0 || a->dim == 0) return MSS_OK;
+    if (!a->x || !a->residual_out || !a->weight || !a->out)
+        return fail(MSS_ERR_INVALID, "add_rms_norm: x, residual_out, weight and out must be non-null");
+    const int es = esize(a->itype);
+    if (!al16(a->x) || !al16(a->residual_out) || !al16(a->weight) || !al16(a->out) ||
+        (a->residual_in && !al16(a->residual_in)) || !st16(a->x_rs, es) || !st16(a->out_rs, es) ||
+        !st16(a->rout_rs, esize(a->rout_type)) || (a->residual_in && !st16(a->rin_rs, esize(a->rin_type))))
+        return fail(MSS_ERR_ALIGNMENT, "add_rms_norm: rows must start on 16-byte boundaries");
+    cudaError_t e = launch_add_rms_norm(*a, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? MSS_OK : cuda_fail(e, "add_rms_norm launch");
+}
+
 }  // extern "C"

@@ -110,6 +110,20 @@ class StateUpdateArgs(ctypes.Structure):
     ]
 
 
+class AddRmsNormArgs(ctypes.Structure):
+    _fields_ = [
+        ("rows", i64), ("dim", i64),
+        ("itype", i32), ("rin_type", i32), ("rout_type", i32), ("wtype", i32),
+        ("x", vp), ("x_rs", i64),
+        ("residual_in", vp), ("rin_rs", i64),
+        ("residual_out", vp), ("rout_rs", i64),
+        ("weight", vp),
+        ("out", vp), ("out_rs", i64),
+        ("rstd", vp),
+        ("eps", ctypes.c_float), ("_pad", i32),
+    ]
+
+
 STRUCTS = (SsFwdArgs, SsBwdArgs, Conv1dArgs, Conv1dUpdateArgs, StateUpdateArgs)
 
 # (name, argtypes, restype) of every symbol the header declares.
@@ -125,6 +139,8 @@ SYMBOLS = [
     ("conv1d_bwd", [ctypes.POINTER(Conv1dArgs), vp], ctypes.c_int),
     ("conv1d_update", [ctypes.POINTER(Conv1dUpdateArgs), vp], ctypes.c_int),
     ("ssm_state_update", [ctypes.POINTER(StateUpdateArgs), vp], ctypes.c_int),
+    ("add_rms_norm", [ctypes.POINTER(AddRmsNormArgs), vp], ctypes.c_int),
+    ("add_rms_norm_args_size", [], i64),
     ("ss_last_error", [], ctypes.c_char_p),
     ("ss_version", [], ctypes.c_char_p),
     ("ss_abi_struct_sizes", [ctypes.POINTER(i64)], None),
@@ -153,6 +169,8 @@ def check_layout():
     for s, st in zip(sizes, STRUCTS):
         if s != ctypes.sizeof(st):
             raise ImportError(f"motif_ssm: {st.__name__} is {ctypes.sizeof(st)} bytes in Python but {s} in the library")
+    if lib.add_rms_norm_args_size() != ctypes.sizeof(AddRmsNormArgs):
+        raise ImportError("motif_ssm: AddRmsNormArgs does not match add_rms_norm_args in the library")
 
 
 check_layout()

@@ -23,6 +23,8 @@ import torch.nn.functional as F
 
 from .causal_conv1d import causal_conv1d_fn, causal_conv1d_update
 from .selective_scan_interface import mamba_inner_fn, selective_scan_fn
+from .norm import add_rms_norm
+from .norm import supported as rms_fused_supported
 from .selective_state_update import selective_state_update
 
 
@@ -262,6 +264,18 @@ class RMSNorm(nn.Module):
         return F.rms_norm(x, (x.shape[-1],), self.weight, self.eps)
 
 
+def add_norm(x, residual, norm, residual_in_fp32=True):
+    """residual <- x + residual, normed <- norm(residual); one fused kernel for RMSNorm
+    (``norm.add_rms_norm``, what the reference's fused_add_norm path computes), the torch
+    expression for LayerNorm or shapes the kernel does not take."""
+    if isinstance(norm, RMSNorm) and rms_fused_supported(x, residual, norm.weight):
+        return add_rms_norm(x, residual, norm.weight, norm.eps, residual_in_fp32)
+    residual = x if residual is None else x + residual
+    if residual_in_fp32:
+        residual = residual.float()
+    return norm(residual.to(norm.weight.dtype)), residual
+
+
 class Block(nn.Module):
     """Add -> Norm -> Mixer (mixer_seq_simple.py:142-146): returns (mixer_out, residual)."""
 
@@ -270,10 +284,7 @@ class Block(nn.Module):
         self.mixer, self.norm, self.residual_in_fp32 = mixer, norm, residual_in_fp32
 
     def forward(self, hidden_states, residual=None, inference_params=None):
-        residual = hidden_states if residual is None else hidden_states + residual
-        hidden_states = self.norm(residual.to(self.norm.weight.dtype))
-        if self.residual_in_fp32:
-            residual = residual.float()
+        hidden_states, residual = add_norm(hidden_states, residual, self.norm, self.residual_in_fp32)
         return self.mixer(hidden_states, inference_params=inference_params), residual
 
     def allocate_inference_cache(self, batch_size, max_seqlen, dtype=None, **kw):
@@ -336,8 +347,7 @@ class MixerModel(nn.Module):
         hidden, residual = self.embedding(input_ids), None
         for layer in self.layers:
             hidden, residual = layer(hidden, residual, inference_params=inference_params)
-        residual = hidden + residual if residual is not None else hidden
-        return self.norm_f(residual.to(self.norm_f.weight.dtype))
+        return add_norm(hidden, residual, self.norm_f)[0]
 
 
 class MambaLMHeadModel(nn.Module):

@@ -173,3 +173,35 @@ def test_mamba_inner_rms_options(which, checkpoint_lvl):
             out.backward(rec["dout"].to(DEV))
             for k in inp:
                 assert_close(dl[k].grad, leaves[k].grad, 1e-3, 1e-3, f"{which} d{k}")
+
+
+@pytest.mark.parametrize("dtype,rdtype,with_res", [(torch.bfloat16, torch.float32, True),
+                                                  (torch.bfloat16, torch.float32, False),
+                                                  (torch.float32, torch.float32, True),
+                                                  (torch.float16, torch.float16, True)])
+def test_add_rms_norm_fused(dtype, rdtype, with_res):
+    """Fused residual add + RMSNorm (the reference stack's fused_add_norm Add -> Norm) against
+    the torch expression in fp32, forward and backward."""
+    from motif_ssm.norm import add_rms_norm
+    g = torch.Generator().manual_seed(4)
+    rows, D = 300, 768
+    x = torch.randn(rows, D, generator=g).to(dtype)
+    res = torch.randn(rows, D, generator=g).to(rdtype) if with_res else None
+    w = (1 + 0.2 * torch.randn(D, generator=g)).to(dtype)
+    dy = torch.randn(rows, D, generator=g).to(dtype)
+    dr = torch.randn(rows, D, generator=g).to(rdtype)
+    leaves = [t.to(DEV).clone().requires_grad_(True) if t is not None else None for t in (x, res, w)]
+    out, rout = add_rms_norm(leaves[0], leaves[1], leaves[2], 1e-5, rdtype == torch.float32)
+    (out.float() * dy.to(DEV).float()).sum().add_((rout.float() * dr.to(DEV).float()).sum()).backward()
+    ref_leaves = [t.float().clone().requires_grad_(True) if t is not None else None for t in (x, res, w)]
+    r = ref_leaves[0] + ref_leaves[1] if with_res else ref_leaves[0]
+    r_st = r.to(rdtype).float() if rdtype != torch.float32 else r
+    ref = r_st * torch.rsqrt(r_st.pow(2).mean(-1, keepdim=True) + 1e-5) * ref_leaves[2]
+    (ref * dy.float()).sum().add_((r * dr.float()).sum()).backward()
+    t = tol(dtype)
+    assert_close(out, ref, t, t, "normed")
+    assert_close(rout, r, t, t, "residual")
+    assert_close(leaves[0].grad, ref_leaves[0].grad, t, t, "dx")
+    if with_res:
+        assert_close(leaves[1].grad, ref_leaves[1].grad, t, t, "dresidual")
+    assert_close(leaves[2].grad, ref_leaves[2].grad, t, t, "dweight")
