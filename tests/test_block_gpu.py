@@ -205,3 +205,27 @@ def test_add_rms_norm_fused(dtype, rdtype, with_res):
     if with_res:
         assert_close(leaves[1].grad, ref_leaves[1].grad, t, t, "dresidual")
     assert_close(leaves[2].grad, ref_leaves[2].grad, t, t, "dweight")
+
+
+def test_layer_norm_module_stand_in():
+    """motif_ssm.layer_norm (registered as mamba_ssm.ops.triton.layer_norm by the shims):
+    _layer_norm_fwd / rms_norm_fn / layer_norm_fn against torch, prenorm and plain, RMS and
+    LayerNorm."""
+    from motif_ssm import layer_norm as LN
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(64, 16, generator=g).bfloat16().to(DEV)
+    w = (1 + 0.1 * torch.randn(16, generator=g)).bfloat16().to(DEV)
+    res = torch.randn(64, 16, generator=g).to(DEV)
+    xf = x.float()
+    ref = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6) * w.float()
+    assert_close(LN._layer_norm_fwd(x, w, None, 1e-6, None, residual_dtype=None, is_rms_norm=True)[0], ref,
+                 2e-2, 2e-2, "rms _layer_norm_fwd")
+    y, r = LN.rms_norm_fn(x, w, None, residual=res, prenorm=True, residual_in_fp32=True, eps=1e-6)
+    rr = xf + res
+    assert_close(r, rr, 1e-6, 1e-6, "prenorm residual")
+    assert_close(y, rr * torch.rsqrt(rr.pow(2).mean(-1, keepdim=True) + 1e-6) * w.float(), 2e-2, 2e-2, "prenorm y")
+    b = (0.1 * torch.randn(16, generator=g)).bfloat16().to(DEV)
+    ln = LN.layer_norm_fn(x, w, b, eps=1e-5)
+    assert_close(ln, torch.nn.functional.layer_norm(xf, (16,), w.float(), b.float(), 1e-5), 2e-2, 2e-2, "layernorm")
+    m = LN.RMSNorm(16, eps=1e-6, device=DEV, dtype=torch.bfloat16)
+    assert_close(m(x), xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6), 2e-2, 2e-2, "RMSNorm module")
