@@ -379,7 +379,7 @@ def issue_ceiling(kernel, ms, clocks):
             "frac": achieved / peak}
 
 
-def run_e2e(t, dout, dev, stream, world, selective_scan_fn, algo, steps, dist, n_sub=8):
+def run_e2e(t, dout, dev, stream, world, selective_scan_fn, algo, steps, dist, n_sub=16):
     """selective_scan_fn (autograd) per step with host buffers: pinned host inputs ->
     device, forward, backward, all 8 gradients -> pinned host, timed with CUDA events
     around the whole step, max over ranks.
