@@ -416,11 +416,12 @@ class TPMambamotif(nn.Module):
         self.A_log = nn.Parameter(torch.empty(d_inner_local, d_state, device=device, dtype=torch.float32))
         self.D = nn.Parameter(torch.empty(d_inner_local, device=device, dtype=torch.float32))
         self.out_proj_w = nn.Parameter(torch.empty(d_model, d_inner_local, **fk))
+        self.P_eff = self.Q = None  # motif coupling: pq_k * P and Q (this rank's channels if per channel)
 
     @classmethod
     def from_full(cls, full, rank, world, group):
-        if full.P is not None:
-            raise NotImplementedError("tensor-parallel sharding of the P/Q coupling is not implemented")
+        """Channel shard `rank` of a full mixer.  A per-channel P / Q is sliced with the
+        channels; a shared one (same for every channel) is replicated."""
         di = full.d_inner
         assert di % world == 0, "d_inner must divide by the tensor-parallel size"
         dl = di // world
@@ -438,6 +439,11 @@ class TPMambamotif(nn.Module):
             m.A_log.copy_(full.A_log[lo:hi])
             m.D.copy_(full.D[lo:hi])
             m.out_proj_w.copy_(full.out_proj.weight[:, lo:hi])
+            if full.P is not None:
+                P_eff, Q = (full.pq_k * full.P).float(), full.Q.float()
+                if full.pq_per_dim:
+                    P_eff, Q = P_eff[lo:hi], Q[lo:hi]
+                m.P_eff, m.Q = P_eff.contiguous(), Q.contiguous()
         return m
 
     def _all_reduce(self, t):
@@ -458,7 +464,7 @@ class TPMambamotif(nn.Module):
         B = B.reshape(batch, seqlen, -1).transpose(1, 2).contiguous()
         C = C.reshape(batch, seqlen, -1).transpose(1, 2).contiguous()
         y = selective_scan_fn(x, dt, -torch.exp(self.A_log), B, C, self.D, z=z, delta_bias=self.dt_proj_b,
-                              delta_softplus=True)
+                              delta_softplus=True, P=self.P_eff, Q=self.Q)
         out = y.transpose(1, 2).reshape(-1, self.d_local) @ self.out_proj_w.t()
         return self._all_reduce(out.contiguous()).view(batch, seqlen, self.d_model)  # all-reduce #2
 

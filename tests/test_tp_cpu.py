@@ -26,9 +26,10 @@ def _patch_ops():
     def conv(x, w, b=None, activation=None):
         return O.causal_conv1d_ref(x, w, b, activation)
 
-    def scan(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softplus=False, return_last_state=False):
+    def scan(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softplus=False, return_last_state=False,
+             P=None, Q=None, gamma=None):
         return O.selective_scan_ref(u, delta, A, B, C, D, z=z, delta_bias=delta_bias,
-                                    delta_softplus=delta_softplus, return_last_state=return_last_state)
+                                    delta_softplus=delta_softplus, return_last_state=return_last_state, P=P, Q=Q)
 
     def inner(*a, **k):
         return O.mamba_inner_ref(*a, **{kk: v for kk, v in k.items() if kk != "checkpoint_lvl"})
@@ -39,7 +40,7 @@ def _patch_ops():
     return modules
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, pq_rank=0, pq_per_dim=False):
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path[:0] = [root, os.path.join(root, "motif-mamba_b200")]
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
@@ -47,8 +48,16 @@ def _worker(rank, world, port, q):
     try:
         modules = _patch_ops()
         torch.manual_seed(0)
-        model = modules.MambaLMHeadModel(modules.MambaConfig(d_model=32, n_layer=2, vocab_size=40,
-                                                             ssm_cfg={"d_state": 8}))
+        model = modules.MambaLMHeadModel(modules.MambaConfig(
+            d_model=32, n_layer=2, vocab_size=40,
+            ssm_cfg={"d_state": 8, "pq_rank": pq_rank, "pq_per_dim": pq_per_dim}))
+        if pq_rank:  # a coupling strong enough to change the outputs
+            g = torch.Generator().manual_seed(3)
+            with torch.no_grad():
+                for layer in model.backbone.layers:
+                    layer.mixer.pq_k.fill_(20.0)
+                    layer.mixer.P.copy_(0.5 * torch.randn(layer.mixer.P.shape, generator=g))
+                    layer.mixer.Q.copy_(0.5 * torch.randn(layer.mixer.Q.shape, generator=g))
         ids = torch.randint(0, 40, (2, 24))
         with torch.no_grad():
             ref = model(ids)
@@ -59,11 +68,15 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_tp2_gloo_matches_unsharded():
+@pytest.mark.parametrize("pq_rank,pq_per_dim", [(0, False), (2, False), (2, True)],
+                         ids=["plain", "pq_shared", "pq_per_channel"])
+def test_tp2_gloo_matches_unsharded(pq_rank, pq_per_dim):
+    """Also with the motif P/Q coupling: a per-channel P / Q is sliced with the channels,
+    a shared one replicated."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, pq_rank, pq_per_dim)) for r in range(2)]
     for p in procs:
         p.start()
     res = [q.get(timeout=240) for _ in procs]
