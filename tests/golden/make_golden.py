@@ -15,9 +15,9 @@ before the file is executed:
 (``nn.Conv1d(groups=d, padding=w-1)[..., :L]`` + SiLU,
 ``motifmamba/mamba_ssm/modules/mamba_simplemotif.py:75-83, 295``).
 
-Run in a container that has the reference at ``$MOTIF_REF`` (default
-``/root/reference/motifmamba``).  The outputs are small ``.pt`` files next to
-this script; nothing at test time reads the reference.
+Run in a container that has the reference checkout (its ``motifmamba`` project directory
+in ``$MOTIF_REF``, default the checkout's usual location below).  The outputs are small
+``.pt`` files next to this script; nothing at test time reads the reference.
 """
 import importlib.util
 import os
