@@ -239,10 +239,11 @@ def main():
     ap.add_argument("--batch", type=int, default=None,
                     help="override the per-GPU batch (profiling a smaller case of the same kernels)")
     ap.add_argument("--seqlen", type=int, default=None, help="override the sequence length")
-    ap.add_argument("--workload", default="scan", choices=["scan", "prefill", "tp"],
+    ap.add_argument("--workload", default="scan", choices=["scan", "prefill", "tp", "pq"],
                     help="scan: selective scan fwd+bwd, config 4 (default); prefill: 24-layer config-2 stack, "
                          "prefill tok/s (global batch 16 x 4096, strong scaling) plus greedy decode tok/s; "
-                         "tp: 64-layer config-3 stack, prefill 1 x 32768 with d_inner sharded over the GPUs")
+                         "tp: 64-layer config-3 stack, prefill 1 x 32768 with d_inner sharded over the GPUs; "
+                         "pq: the motif P/Q-coupled scan fwd+bwd at a config-1 block's shape")
     args = ap.parse_args()
     if args.batch:
         CFG["batch"] = args.batch
@@ -253,6 +254,8 @@ def main():
         return run_prefill(args)
     if args.workload == "tp":
         return run_tp(args)
+    if args.workload == "pq":
+        return run_pq(args)
     if args.impl == "reference":
         return run_reference(args)
 
@@ -605,6 +608,124 @@ def run_prefill(args):
             "e2e": {"value": bl * world * P["seqlen"] / (te.item() * 1e-3), "unit": "tok/s",
                     "h2d_bytes_per_step": host_ids.numel() * 8, "d2h_bytes_per_step": out_host.numel() * 2},
             "cpu_baseline": cpu}), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+PQ = dict(batch=8, dim=1536, seqlen=2048, dstate=16, rank=4)
+
+
+def _pq_inputs(b, d, l, n, r, device, seed, dtype=torch.bfloat16):
+    g = torch.Generator(device=device).manual_seed(seed)
+    rn = lambda *sh: torch.randn(*sh, device=device, generator=g)
+    t = dict(u=rn(b, d, l).to(dtype), delta=rn(b, d, l).to(dtype), z=rn(b, d, l).to(dtype),
+             B=rn(b, 1, n, l).to(dtype), C=rn(b, 1, n, l).to(dtype),
+             A=-torch.arange(1, n + 1, device=device, dtype=torch.float32).repeat(d, 1),
+             D=1 + 0.1 * rn(d), delta_bias=torch.log(torch.expm1(torch.rand(d, device=device, generator=g) * 0.099 + 1e-3)),
+             P=0.1 * rn(n, r), Q=0.1 * rn(r, n))
+    return t, rn(b, d, l).to(dtype)
+
+
+def _cpu_pq_record(threads, budget_s):
+    """The reference's CPU path for the P/Q scan (oracle restatement of selective_scan_ref with
+    P / Q, fwd + autograd bwd) on batch 1 x a channel slice x the full sequence."""
+    from oracle import ssm_oracle as O
+    torch.set_num_threads(threads)
+    l, n, r = PQ["seqlen"], PQ["dstate"], PQ["rank"]
+
+    def run(dim_s):
+        t, dout = _pq_inputs(1, dim_s, l, n, r, "cpu", 0)
+        t = {k: v for k, v in t.items()}
+        t["B"], t["C"] = t["B"][:, 0], t["C"][:, 0]
+        t0 = time.perf_counter()
+        O.scan_with_grads(t, dout, True)
+        return time.perf_counter() - t0
+
+    probe = 4
+    tp = run(probe)
+    dim_s = int(max(probe, min(PQ["dim"], probe * budget_s / max(tp, 1e-3))))
+    dt = run(dim_s)
+    el = dim_s * l * n
+    return dict(value=el / dt / 1e9, unit="G element-states/s", cores=threads, kind="port",
+                sample=f"selective_scan_ref with P / Q (rank {r}, shared), fwd + autograd bwd, batch 1 x {dim_s} "
+                       f"channels x seqlen {l}, n {n}, bf16 inputs, fp32 math: {dt:.2f} s")
+
+
+def run_pq(args):
+    """The motif P/Q-coupled scan, fwd + bwd (all gradients incl. dP, dQ), at a config-1 block's
+    shape (batch 8, d_inner 1536, seqlen 2048, n 16, rank 4 shared, bf16, z), per GPU (weak
+    scaling; no collective).  Metric: element-states (batch x d_inner x seqlen x dstate) per
+    second of fwd+bwd."""
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    metric = "P/Q selective-scan fwd+bwd element-states/s"
+    cfg = {"workload": "motif P/Q scan fwd+bwd, 8 x 1536 x 2048 per GPU, n 16, rank 4 shared P/Q, bf16 I/O, z, "
+                       "D, delta_bias, softplus", **PQ,
+           "l2": "working set per step ~0.45 GB (9 tensors of 50 MB) > 126 MB L2, no flush"}
+    if args.impl == "reference":
+        if rank == 0:
+            cb = _cpu_pq_record(os.cpu_count() or 1, 20.0)
+            print(json.dumps({"impl": "reference", "metric": metric, "value": cb["value"], "unit": cb["unit"],
+                              "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+                              "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                              "config": cfg, "cpu_baseline": cb,
+                              "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0,
+                                      "d2h_bytes_per_step": 0}}))
+        return 0
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    from motif_ssm import selective_scan_cuda as ssc
+    b, d, l, n, r = PQ["batch"], PQ["dim"], PQ["seqlen"], PQ["dstate"], PQ["rank"]
+    t, dout = _pq_inputs(b, d, l, n, r, dev, 77 + rank)
+    stream = torch.cuda.current_stream(dev)
+    dP, dQ = torch.empty_like(t["P"]), torch.empty_like(t["Q"])
+
+    def step(ev=None):
+        if ev is not None:
+            ev[0].record(stream)
+        out, x, out_z = ssc.fwd(t["u"], t["delta"], t["A"], t["B"], t["C"], D=t["D"], z=t["z"],
+                                delta_bias=t["delta_bias"], P=t["P"], Q=t["Q"], delta_softplus=True)
+        if ev is not None:
+            ev[1].record(stream)
+        ssc.bwd(t["u"], t["delta"], t["A"], t["B"], t["C"], D=t["D"], z=t["z"], delta_bias=t["delta_bias"],
+                P=t["P"], Q=t["Q"], dout=dout, x=x, out=out, dz=None, dP_out=dP, dQ_out=dQ, delta_softplus=True,
+                recompute_out_z=False)
+        if ev is not None:
+            ev[2].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    with ClockSampler(local) as clk:
+        s.record(stream)
+        for i in range(args.steps):
+            step(evs[i])
+        e.record(stream)
+        torch.cuda.synchronize()
+    tt = torch.tensor([s.elapsed_time(e) / args.steps], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    ms = tt.item()
+    fwd_ms = statistics.median(a.elapsed_time(bq) for a, bq, _ in evs)
+    bwd_ms = statistics.median(bq.elapsed_time(c) for _, bq, c in evs)
+    el = b * d * l * n
+    cpu = _cpu_pq_record(os.cpu_count() or 1, 15.0) if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
+    if rank == 0:
+        print(json.dumps({"metric": metric, "value": el * world / (ms * 1e-3) / 1e9, "unit": "G element-states/s",
+                          "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+                          "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                          "data": "synthetic", "config": cfg,
+                          "kernels": {"ss_pq_fwd": {"ms": fwd_ms}, "ss_pq_bwd": {"ms": bwd_ms}},
+                          "gpu_launches": 4 * args.steps, "clocks": clk.summary(), "e2e": None, "cpu_baseline": cpu}))
     if world > 1:
         dist.destroy_process_group()
     return 0
