@@ -642,10 +642,14 @@ def _cpu_pq_record(threads, budget_s):
         O.scan_with_grads(t, dout, True)
         return time.perf_counter() - t0
 
-    probe = 4
+    probe = 8
+    run(probe)  # warm-up (first-call costs would skew the extrapolation)
     tp = run(probe)
     dim_s = int(max(probe, min(PQ["dim"], probe * budget_s / max(tp, 1e-3))))
     dt = run(dim_s)
+    if dt < 0.5 * budget_s and dim_s < PQ["dim"]:  # per-step overheads do not scale with channels
+        dim_s = int(min(PQ["dim"], dim_s * budget_s / dt))
+        dt = run(dim_s)
     el = dim_s * l * n
     return dict(value=el / dt / 1e9, unit="G element-states/s", cores=threads, kind="port",
                 sample=f"selective_scan_ref with P / Q (rank {r}, shared), fwd + autograd bwd, batch 1 x {dim_s} "
