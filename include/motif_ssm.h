@@ -182,6 +182,16 @@ typedef struct {
     float eps;                  int32_t _pad;
 } add_rms_norm_args;
 
+/* dt_proj folded into the decode state update: dt[b, c] = sum_k weight[c, k] * dt_in[b, k],
+ * rounded to itype (as the separate dt_proj GEMM stores it), then ssm_state_update with that
+ * dt.  weight (dim, rank) contiguous in itype, rank % 8 == 0 and <= 256; dt_in rows of `rank`
+ * elements of itype with 16-byte-aligned starts.  Needs dstate == 16 and the unit-stride,
+ * 16-byte-aligned state / A / B / C rows of ssm_state_update's vector path. */
+typedef struct {
+    const void *dt_in;  int64_t dt_in_bs;   /* (batch, rank) */
+    const void *weight; int64_t rank;       /* (dim, rank) */
+} ssm_dtproj_args;
+
 /* Workspace bytes ss_fwd / ss_bwd need for these arguments (0 means none). */
 MSS_API int ss_fwd_workspace_size(const ss_fwd_args *a, int64_t *bytes);
 MSS_API int ss_bwd_workspace_size(const ss_bwd_args *a, int64_t *bytes);
@@ -218,6 +228,10 @@ MSS_API int ssm_state_update(const ssm_state_update_args *a, void *stream);
 MSS_API int add_rms_norm(const add_rms_norm_args *a, void *stream);
 /* sizeof(add_rms_norm_args), for binding-side layout checks. */
 MSS_API int64_t add_rms_norm_args_size(void);
+
+/* ssm_state_update with dt_proj folded in (the reference step's F.linear(dt, dt_proj.weight)
+ * followed by selective_state_update, mamba_simplemotif.py:363-399); a->dt is not read. */
+MSS_API int ssm_state_update_dtproj(const ssm_state_update_args *a, const ssm_dtproj_args *p, void *stream);
 
 /* Message of the last failure on the calling thread ("" if none). */
 MSS_API const char *ss_last_error(void);

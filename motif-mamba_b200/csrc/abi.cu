@@ -381,8 +381,26 @@ int ssm_state_update(const ssm_state_update_args *a, void *stream) {
     if (a->batch * a->dim == 0) return MSS_OK;
     if (!a->state || !a->x || !a->dt || !a->A || !a->B || !a->C || !a->out)
         return fail(MSS_ERR_INVALID, "ssm_state_update: state, x, dt, A, B, C and out must be non-null");
-    cudaError_t e = launch_state_update(*a, static_cast<cudaStream_t>(stream));
+    cudaError_t e = launch_state_update(*a, nullptr, static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? MSS_OK : cuda_fail(e, "ssm_state_update launch");
+}
+
+int ssm_state_update_dtproj(const ssm_state_update_args *a, const ssm_dtproj_args *p, void *stream) {
+    if (!a || !p) return fail(MSS_ERR_INVALID, "ssm_state_update_dtproj: null argument struct");
+    if (!valid_type(a->itype) || !valid_type(a->stype))
+        return fail(MSS_ERR_INVALID, "ssm_state_update_dtproj: bad element type");
+    if (a->dstate != 16) return fail(MSS_ERR_UNSUPPORTED, "ssm_state_update_dtproj: dstate must be 16");
+    if (a->n_groups < 1 || a->dim % a->n_groups != 0)
+        return fail(MSS_ERR_INVALID, "ssm_state_update_dtproj: n_groups must divide dim");
+    if (p->rank < 8 || p->rank % 8 != 0 || p->rank > 256)
+        return fail(MSS_ERR_UNSUPPORTED, "ssm_state_update_dtproj: rank must be a multiple of 8 in [8, 256]");
+    if (a->batch * a->dim == 0) return MSS_OK;
+    if (!a->state || !a->x || !p->dt_in || !p->weight || !a->A || !a->B || !a->C || !a->out)
+        return fail(MSS_ERR_INVALID, "ssm_state_update_dtproj: a required pointer is null");
+    cudaError_t e = launch_state_update(*a, p, static_cast<cudaStream_t>(stream));
+    if (e == cudaErrorInvalidValue)
+        return fail(MSS_ERR_ALIGNMENT, "ssm_state_update_dtproj: rows must be unit-stride and 16-byte aligned");
+    return e == cudaSuccess ? MSS_OK : cuda_fail(e, "ssm_state_update_dtproj launch");
 }
 
 int64_t add_rms_norm_args_size(void) { return (int64_t)sizeof(add_rms_norm_args); }

@@ -16,15 +16,33 @@ namespace mss {
 // Fast path for the common layout: 16 states, every per-state row (state, A, B, C) unit
 // stride and 16-byte aligned, so each thread moves its rows with 16-byte vector accesses
 // (a warp touches whole sectors) instead of 16 scalar strided ones.
-template <typename T, typename ST>
-__global__ void __launch_bounds__(128) state_update16_vec_kernel(const ssm_state_update_args a) {
+// With DTP the dt of each channel is the dt_proj product of the row's dt inputs (folded in;
+// rounded to T like the GEMM's output), otherwise it is read from a.dt.
+template <typename T, typename ST, bool DTP>
+__global__ void __launch_bounds__(128) state_update16_vec_kernel(const ssm_state_update_args a,
+                                                                 const ssm_dtproj_args dp) {
     constexpr int NS = 16;
     const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     if (i >= a.batch * a.dim) return;
     const int64_t b = i / a.dim, d = i - b * a.dim;
     const int64_t g = d / (a.dim / a.n_groups);
     const float xv = to_f<T>(reinterpret_cast<const T *>(a.x)[b * a.x_bs + d]);
-    float dt = to_f<T>(reinterpret_cast<const T *>(a.dt)[b * a.dt_bs + d]);
+    float dt;
+    if constexpr (DTP) {
+        const T *w = reinterpret_cast<const T *>(dp.weight) + d * dp.rank;
+        const T *di = reinterpret_cast<const T *>(dp.dt_in) + b * dp.dt_in_bs;
+        float acc = 0.f;
+        for (int64_t k0 = 0; k0 < dp.rank; k0 += 8) {
+            float w8[8], x8[8];
+            Vec8<T>::load(w + k0, w8);
+            Vec8<T>::load(di + k0, x8);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) acc = fmaf(w8[k], x8[k], acc);
+        }
+        dt = to_f<T>(from_f<T>(acc));
+    } else {
+        dt = to_f<T>(reinterpret_cast<const T *>(a.dt)[b * a.dt_bs + d]);
+    }
     if (a.dt_bias) dt += a.dt_bias[d];
     if (a.dt_softplus) dt = softplus20(dt);
     const T *Bp = reinterpret_cast<const T *>(a.B) + b * a.B_bs + g * a.B_gs;
@@ -113,18 +131,31 @@ __global__ void __launch_bounds__(128) state_update_kernel(const ssm_state_updat
 }
 
 template <typename T, typename ST>
-static cudaError_t su_st(const ssm_state_update_args &a, cudaStream_t st) {
+static bool su_vec_ok(const ssm_state_update_args &a) {
+    auto al16 = [](const void *q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+    return a.dstate == 16 && a.st_ns == 1 && a.A_ns == 1 && al16(a.state) && al16(a.A) && al16(a.B) && al16(a.C) &&
+           (a.st_bs * sizeof(ST)) % 16 == 0 && (a.st_ds * sizeof(ST)) % 16 == 0 && (a.A_ds * 4) % 16 == 0 &&
+           (a.B_bs * sizeof(T)) % 16 == 0 && (a.B_gs * sizeof(T)) % 16 == 0 && (a.C_bs * sizeof(T)) % 16 == 0 &&
+           (a.C_gs * sizeof(T)) % 16 == 0;
+}
+
+template <typename T, typename ST>
+static cudaError_t su_st(const ssm_state_update_args &a, const ssm_dtproj_args *dp, cudaStream_t st) {
     const int64_t n = a.batch * a.dim;
     const int threads = 128;
     const unsigned blocks = (unsigned)((n + threads - 1) / threads);
     if (n == 0) return cudaSuccess;
-    auto al16 = [](const void *q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
-    const bool vec = a.dstate == 16 && a.st_ns == 1 && a.A_ns == 1 && al16(a.state) && al16(a.A) && al16(a.B) &&
-                     al16(a.C) && (a.st_bs * sizeof(ST)) % 16 == 0 && (a.st_ds * sizeof(ST)) % 16 == 0 &&
-                     (a.A_ds * 4) % 16 == 0 && (a.B_bs * sizeof(T)) % 16 == 0 && (a.B_gs * sizeof(T)) % 16 == 0 &&
-                     (a.C_bs * sizeof(T)) % 16 == 0 && (a.C_gs * sizeof(T)) % 16 == 0;
+    const bool vec = su_vec_ok<T, ST>(a);
+    if (dp) {
+        auto al16 = [](const void *q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+        if (!vec || dp->rank % 8 != 0 || dp->rank > 256 || !al16(dp->weight) || !al16(dp->dt_in) ||
+            (dp->dt_in_bs * sizeof(T)) % 16 != 0)
+            return cudaErrorInvalidValue;
+        state_update16_vec_kernel<T, ST, true><<<blocks, threads, 0, st>>>(a, *dp);
+        return cudaGetLastError();
+    }
     if (vec)
-        state_update16_vec_kernel<T, ST><<<blocks, threads, 0, st>>>(a);
+        state_update16_vec_kernel<T, ST, false><<<blocks, threads, 0, st>>>(a, ssm_dtproj_args{});
     else if (a.dstate <= 16)
         state_update_kernel<T, ST, 16><<<blocks, threads, 0, st>>>(a);
     else if (a.dstate <= 32)
@@ -136,18 +167,18 @@ static cudaError_t su_st(const ssm_state_update_args &a, cudaStream_t st) {
     return cudaGetLastError();
 }
 template <typename T>
-static cudaError_t su_t(const ssm_state_update_args &a, cudaStream_t st) {
+static cudaError_t su_t(const ssm_state_update_args &a, const ssm_dtproj_args *dp, cudaStream_t st) {
     switch (a.stype) {
-        case MSS_F32: return su_st<T, float>(a, st);
-        case MSS_F16: return su_st<T, __half>(a, st);
-        default: return su_st<T, __nv_bfloat16>(a, st);
+        case MSS_F32: return su_st<T, float>(a, dp, st);
+        case MSS_F16: return su_st<T, __half>(a, dp, st);
+        default: return su_st<T, __nv_bfloat16>(a, dp, st);
     }
 }
-cudaError_t launch_state_update(const ssm_state_update_args &a, cudaStream_t st) {
+cudaError_t launch_state_update(const ssm_state_update_args &a, const ssm_dtproj_args *dp, cudaStream_t st) {
     switch (a.itype) {
-        case MSS_F32: return su_t<float>(a, st);
-        case MSS_F16: return su_t<__half>(a, st);
-        default: return su_t<__nv_bfloat16>(a, st);
+        case MSS_F32: return su_t<float>(a, dp, st);
+        case MSS_F16: return su_t<__half>(a, dp, st);
+        default: return su_t<__nv_bfloat16>(a, dp, st);
     }
 }
 

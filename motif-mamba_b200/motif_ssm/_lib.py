@@ -124,6 +124,10 @@ class AddRmsNormArgs(ctypes.Structure):
     ]
 
 
+class DtProjArgs(ctypes.Structure):
+    _fields_ = [("dt_in", vp), ("dt_in_bs", i64), ("weight", vp), ("rank", i64)]
+
+
 STRUCTS = (SsFwdArgs, SsBwdArgs, Conv1dArgs, Conv1dUpdateArgs, StateUpdateArgs)
 
 # (name, argtypes, restype) of every symbol the header declares.
@@ -139,6 +143,7 @@ SYMBOLS = [
     ("conv1d_bwd", [ctypes.POINTER(Conv1dArgs), vp], ctypes.c_int),
     ("conv1d_update", [ctypes.POINTER(Conv1dUpdateArgs), vp], ctypes.c_int),
     ("ssm_state_update", [ctypes.POINTER(StateUpdateArgs), vp], ctypes.c_int),
+    ("ssm_state_update_dtproj", [ctypes.POINTER(StateUpdateArgs), ctypes.POINTER(DtProjArgs), vp], ctypes.c_int),
     ("add_rms_norm", [ctypes.POINTER(AddRmsNormArgs), vp], ctypes.c_int),
     ("add_rms_norm_args_size", [], i64),
     ("ss_last_error", [], ctypes.c_char_p),

@@ -25,7 +25,7 @@ from .causal_conv1d import causal_conv1d_fn, causal_conv1d_update
 from .selective_scan_interface import mamba_inner_fn, selective_scan_fn
 from .norm import add_rms_norm
 from .norm import supported as rms_fused_supported
-from .selective_state_update import selective_state_update
+from .selective_state_update import dtproj_supported, selective_state_update, selective_state_update_dtproj
 
 
 class Mambamotif(nn.Module):
@@ -215,6 +215,12 @@ class Mambamotif(nn.Module):
                                  self.activation)
         x_db = self.x_proj(x)
         dt, B, C = torch.split(x_db, [self.dt_rank, self.d_state, self.d_state], dim=-1)
+        if self.P is None and dtproj_supported(ssm_state, x, dt, self.dt_proj.weight):
+            # dt_proj folded into the state update kernel (same rounding of dt as the GEMM)
+            A, dt_bias = self._decode_consts()
+            y = selective_state_update_dtproj(ssm_state, x, dt, self.dt_proj.weight, A, B, C, self.D, z=z,
+                                              dt_bias=dt_bias, dt_softplus=True)
+            return self.out_proj(y).unsqueeze(1), conv_state, ssm_state
         dt = F.linear(dt, self.dt_proj.weight)
         if self.P is not None:
             A = -torch.exp(self.A_log.float())

@@ -16,11 +16,43 @@ def selective_state_update(state, x, dt, A, B, C, D=None, z=None, dt_bias=None, 
                            state_batch_indices=None):
     if state_batch_indices is not None:
         raise NotImplementedError("selective_state_update: state_batch_indices is not supported")
+    a, out = _state_args(state, x, dt, A, B, C, D, z, dt_bias, dt_softplus)
+    with torch.cuda.device(x.device):
+        check(lib.ssm_state_update(ctypes.byref(a), _stream(x.device)))
+    return out
+
+
+def dtproj_supported(state, x, dt_in, dt_proj_weight):
+    """Whether ``selective_state_update_dtproj`` takes these tensors."""
+    r = dt_proj_weight.shape[-1]
+    return (state.dim() == 3 and state.shape[-1] == 16 and state.is_contiguous() and r % 8 == 0 and r <= 256
+            and dt_proj_weight.is_contiguous() and dt_proj_weight.dtype == x.dtype == dt_in.dtype
+            and dt_in.stride(-1) == 1 and (dt_in.stride(0) * dt_in.element_size()) % 16 == 0
+            and dt_in.data_ptr() % 16 == 0 and dt_proj_weight.data_ptr() % 16 == 0)
+
+
+def selective_state_update_dtproj(state, x, dt_in, dt_proj_weight, A, B, C, D=None, z=None, dt_bias=None,
+                                  dt_softplus=False):
+    """``selective_state_update(state, x, F.linear(dt_in, dt_proj_weight), ...)`` in one kernel
+    (the decode step's dt_proj GEMM folded into the state update; dt is rounded to x's dtype
+    as the GEMM output is).  dt_in (batch, dt_rank), dt_proj_weight (dim, dt_rank)."""
+    batch = x.shape[0]
+    dim, rank = dt_proj_weight.shape
+    _req(dt_in.shape == (batch, rank), "dt_in must be (batch, dt_rank)")
+    a, out = _state_args(state, x, None, A, B, C, D, z, dt_bias, dt_softplus)
+    p = _lib.DtProjArgs()
+    p.dt_in, p.dt_in_bs, p.weight, p.rank = _ptr(dt_in), dt_in.stride(0), _ptr(dt_proj_weight), rank
+    with torch.cuda.device(x.device):
+        check(lib.ssm_state_update_dtproj(ctypes.byref(a), ctypes.byref(p), _stream(x.device)))
+    return out
+
+
+def _state_args(state, x, dt, A, B, C, D, z, dt_bias, dt_softplus):
     if state.dim() != 3:
         raise NotImplementedError("selective_state_update: only the (batch, dim, dstate) layout is supported")
     batch, dim, dstate = state.shape
-    _req(x.shape == (batch, dim) and dt.shape == (batch, dim), "x and dt must be (batch, dim)")
-    _req(x.dtype == dt.dtype, "x and dt must share a dtype")
+    _req(x.shape == (batch, dim) and (dt is None or dt.shape == (batch, dim)), "x and dt must be (batch, dim)")
+    _req(dt is None or x.dtype == dt.dtype, "x and dt must share a dtype")
     _req(A.shape == (dim, dstate) and A.dtype == torch.float32, "A must be float32 (dim, dstate)")
     if B.dim() == 2:
         B = B.unsqueeze(1)
@@ -38,7 +70,7 @@ def selective_state_update(state, x, dt, A, B, C, D=None, z=None, dt_bias=None, 
     if C.stride(-1) != 1:
         C = C.contiguous()
     for t in (x, dt):
-        _req(t.stride(-1) == 1, "x and dt must have unit stride in the last dimension")
+        _req(t is None or t.stride(-1) == 1, "x and dt must have unit stride in the last dimension")
     if D is not None:
         D = D.float().contiguous()
         _req(D.shape == (dim,), "D must be (dim,)")
@@ -55,7 +87,8 @@ def selective_state_update(state, x, dt, A, B, C, D=None, z=None, dt_bias=None, 
     a.itype, a.stype, a.dt_softplus = _itype(x.dtype), _itype(state.dtype), 1 if dt_softplus else 0
     a.state, a.st_bs, a.st_ds, a.st_ns = _ptr(state), state.stride(0), state.stride(1), state.stride(2)
     a.x, a.x_bs = _ptr(x), x.stride(0)
-    a.dt, a.dt_bs = _ptr(dt), dt.stride(0)
+    if dt is not None:
+        a.dt, a.dt_bs = _ptr(dt), dt.stride(0)
     a.A, a.A_ds, a.A_ns = _ptr(A), A.stride(0), A.stride(1)
     a.B, a.B_bs, a.B_gs = _ptr(B), B.stride(0), B.stride(1)
     a.C, a.C_bs, a.C_gs = _ptr(C), C.stride(0), C.stride(1)
@@ -64,6 +97,4 @@ def selective_state_update(state, x, dt, A, B, C, D=None, z=None, dt_bias=None, 
         a.z, a.z_bs = _ptr(z), z.stride(0)
     a.dt_bias = _ptr(dt_bias)
     a.out, a.out_bs = _ptr(out), out.stride(0)
-    with torch.cuda.device(x.device):
-        check(lib.ssm_state_update(ctypes.byref(a), _stream(x.device)))
-    return out
+    return a, out

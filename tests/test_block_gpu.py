@@ -229,3 +229,28 @@ def test_layer_norm_module_stand_in():
     assert_close(ln, torch.nn.functional.layer_norm(xf, (16,), w.float(), b.float(), 1e-5), 2e-2, 2e-2, "layernorm")
     m = LN.RMSNorm(16, eps=1e-6, device=DEV, dtype=torch.bfloat16)
     assert_close(m(x), xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6), 2e-2, 2e-2, "RMSNorm module")
+
+
+@pytest.mark.parametrize("dtype,state_dtype", [(torch.bfloat16, torch.bfloat16), (torch.float32, torch.float32)])
+def test_state_update_with_dtproj_folded_in(dtype, state_dtype):
+    """ssm_state_update_dtproj == F.linear(dt_in, W) followed by selective_state_update (the
+    decode step's dt_proj GEMM folded into the state update), config-2 decode shape."""
+    from motif_ssm.selective_state_update import selective_state_update, selective_state_update_dtproj
+    batch, dim, n, r = 64, 1536, 16, 48
+    g = torch.Generator().manual_seed(5)
+    x_db = torch.randn(batch, r + 2 * n, generator=g).to(dtype).to(DEV)   # dt_in, B, C as views of one row
+    dt_in, B, C = torch.split(x_db, [r, n, n], dim=-1)
+    W = ((r ** -0.5) * torch.randn(dim, r, generator=g)).to(dtype).to(DEV)
+    x = torch.randn(batch, dim, generator=g).to(dtype).to(DEV)
+    z = torch.randn(batch, dim, generator=g).to(dtype).to(DEV)
+    A = -torch.arange(1, n + 1, dtype=torch.float32).repeat(dim, 1).to(DEV)
+    D = torch.randn(dim, generator=g).to(DEV)
+    dt_bias = torch.randn(dim, generator=g).to(DEV)
+    st0 = torch.randn(batch, dim, n, generator=g).to(state_dtype).to(DEV)
+    s1, s2 = st0.clone(), st0.clone()
+    ref = selective_state_update(s1, x, torch.nn.functional.linear(dt_in, W), A, B, C, D, z=z, dt_bias=dt_bias,
+                                 dt_softplus=True)
+    out = selective_state_update_dtproj(s2, x, dt_in, W, A, B, C, D, z=z, dt_bias=dt_bias, dt_softplus=True)
+    t = tol(dtype)
+    assert_close(out, ref, t, t, "y")
+    assert_close(s2, s1, t, t, "state")
