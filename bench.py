@@ -528,10 +528,11 @@ def run_prefill(args):
     g = torch.Generator(device=dev).manual_seed(rank)
     ids = torch.randint(0, P["vocab"], (bl, P["seqlen"]), device=dev, generator=g)
     stream = torch.cuda.current_stream(dev)
+    from motif_ssm.modules import GraphedForward
+    graphed = GraphedForward(model, bl, P["seqlen"])  # the whole prefill as one CUDA graph
 
     def prefill():
-        with torch.no_grad():
-            return model(ids, num_last_tokens=1)
+        return graphed(ids)
 
     for _ in range(args.warmup):
         prefill()
@@ -585,8 +586,7 @@ def run_prefill(args):
     s.record(stream)
     for _ in range(args.steps):
         dev_ids.copy_(host_ids, non_blocking=True)
-        with torch.no_grad():
-            lg = model(dev_ids, num_last_tokens=1)
+        lg = graphed(dev_ids)
         out_host.copy_(lg, non_blocking=True)
     e.record(stream)
     torch.cuda.synchronize()
@@ -601,7 +601,8 @@ def run_prefill(args):
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "24-layer MotifMamba stack (d_model 768, d_inner 1536, n 16, RMSNorm, vocab 512), "
                                    "bf16 random init, prefill of global batch 16 x 4096 random ids, last-token logits",
-                       "global_batch": bl * world, "seqlen": P["seqlen"], "parallelism": f"batch-sharded x{world}"},
+                       "global_batch": bl * world, "seqlen": P["seqlen"], "parallelism": f"batch-sharded x{world}",
+                       "cuda_graph": True},
             "decode_tok_s": decode_tok_s, "decode": {"global_batch": db * world, "steps": P["decode_steps"],
                                                      "prompt": P["prompt"], "cuda_graph": True},
             "gpu_launches": None, "clocks": clk.summary(),

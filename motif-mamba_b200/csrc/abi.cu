@@ -45,10 +45,15 @@ struct FwdShape {
 FwdShape fwd_shape(const ss_fwd_args *a) {
     FwdShape s{1, (int)a->seqlen, 0, 0};
     const int64_t rows = a->batch * a->dim;
-    const int64_t target = (int64_t)kNumSMs * 512;  // resident threads wanted
-    if (!a->P && rows > 0 && rows < target && a->seqlen > 2 * kChunkLen) {
-        int64_t want = (target + rows - 1) / rows;
-        int64_t seg = round_up((a->seqlen + want - 1) / want, kChunkLen);
+    // Few rows (small batch x channels): split the sequence into segments so that rows x
+    // segments fills up to one wave of resident threads (6 CTAs of 128 per SM for dstate <= 16);
+    // segments are whole 16-step tiles.  A carry pass gives every segment its initial state.
+    const int64_t capacity = (int64_t)kNumSMs * (a->dstate <= 16 ? 768 : 128);
+    const int64_t n_want = rows > 0 ? capacity / rows : 1;
+    if (!a->P && rows > 0 && n_want >= 2 && a->seqlen >= 4 * 64) {
+        // at most 16 segments (every segment folds the carries of the earlier ones) of >= 64 steps
+        const int64_t n_max = std::min<int64_t>(std::min<int64_t>(n_want, 16), a->seqlen / 64);
+        int64_t seg = round_up((a->seqlen + n_max - 1) / n_max, 16);
         int64_t n = (a->seqlen + seg - 1) / seg;
         if (n > 1) {
             s.n_seg = (int)n;

@@ -101,13 +101,27 @@ __global__ void __launch_bounds__(FwdCfg<NS>::CH, FwdCfg<NS>::MINB) ss_fwd_kerne
     float cum = 0.f;  // sum of dt since t = 0 (main pass) or since the segment start (carry pass)
     const int64_t row = (int64_t)b * p.dim + d;
     if (!CARRY && s > 0 && valid) {
+        // fold the carries of the earlier segments: h = decay(segment) h + H(segment)
         for (int sp = 0; sp < s; ++sp) {
             const float dts = p.ws_dts[row * p.n_seg + sp];
             const float *H = p.ws_h + (row * p.n_seg + sp) * NS;
+            if (chain) {  // decay of state n over the segment = R^(n+1), R = exp(A_0 dts)
+                const float R = ex2(A2[0] * dts);
+                float pw = R;
 #pragma unroll
-            for (int m = 0; m < NP; ++m) {
-                const float2 hv = unpack2(h2[m]);
-                h2[m] = pack2(fmaf(ex2(A2[2 * m] * dts), hv.x, H[2 * m]), fmaf(ex2(A2[2 * m + 1] * dts), hv.y, H[2 * m + 1]));
+                for (int m = 0; m < NP; ++m) {
+                    const float2 hv = unpack2(h2[m]);
+                    const float p0 = pw, p1 = pw * R;
+                    pw = p1 * R;
+                    h2[m] = pack2(fmaf(p0, hv.x, H[2 * m]), fmaf(p1, hv.y, H[2 * m + 1]));
+                }
+            } else {
+#pragma unroll
+                for (int m = 0; m < NP; ++m) {
+                    const float2 hv = unpack2(h2[m]);
+                    h2[m] = pack2(fmaf(ex2(A2[2 * m] * dts), hv.x, H[2 * m]),
+                                  fmaf(ex2(A2[2 * m + 1] * dts), hv.y, H[2 * m + 1]));
+                }
             }
             cum += dts;
         }

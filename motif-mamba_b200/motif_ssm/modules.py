@@ -483,6 +483,32 @@ def shard_model_tp(model, rank, world, group=None):
     return model
 
 
+class GraphedForward:
+    """A no-cache forward of a MambaLMHeadModel (prefill) for one fixed input shape, captured as
+    a CUDA graph, so that short or small-batch prefills are not bound by the host launching
+    ~15 kernels per layer.  ``out = gf(ids)`` copies ids into the static input buffer, replays
+    and returns the static output buffer (valid until the next call)."""
+
+    def __init__(self, model, batch, seqlen, num_last_tokens=1, warmup=2):
+        self.model = model
+        dev = model.lm_head.weight.device
+        self.ids = torch.zeros(batch, seqlen, dtype=torch.long, device=dev)
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s), torch.no_grad():
+            for _ in range(warmup):
+                model(self.ids, num_last_tokens=num_last_tokens)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph), torch.no_grad():
+            self.out = model(self.ids, num_last_tokens=num_last_tokens)
+
+    def __call__(self, ids):
+        self.ids.copy_(ids)
+        self.graph.replay()
+        return self.out
+
+
 class GraphedDecoder:
     """One decode step of a MambaLMHeadModel captured as a CUDA graph.
 

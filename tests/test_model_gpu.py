@@ -165,3 +165,16 @@ def test_pq_mixer_trains_pq_only():
     (O.mixer_pq_prefill_ref(sd, hs) * w).sum().backward()
     for k in ("P", "Q", "pq_k"):
         assert_close(getattr(mod, k).grad, sd[k].grad, 1e-3, 1e-3, f"d{k}")
+
+
+def test_graphed_prefill_matches_eager():
+    from motif_ssm.modules import GraphedForward, MambaConfig, MambaLMHeadModel
+    torch.manual_seed(11)
+    model = MambaLMHeadModel(MambaConfig(d_model=128, n_layer=2, vocab_size=64, ssm_cfg={"d_state": 16}),
+                             device=DEV, dtype=torch.bfloat16)
+    gf = GraphedForward(model, 2, 600)
+    for seed in (0, 1):
+        ids = torch.randint(0, 64, (2, 600), device=DEV, generator=torch.Generator(device=DEV).manual_seed(seed))
+        with torch.no_grad():
+            eager = model(ids, num_last_tokens=1)
+        assert torch.equal(gf(ids), eager), seed
