@@ -31,9 +31,12 @@
 namespace mss {
 
 template <int NS> struct FwdCfg {
-    static constexpr int CH = NS <= 16 ? 128 : 64;  // channels (threads) per CTA
+    // channels (threads) per CTA: 96 x 8 resident CTAs per SM; at config 4 the 1024 CTAs
+    // spread as 6 or 7 per SM (128-channel CTAs would leave 5 or 6, the SMs with 6 setting the
+    // pace at 86 % of the mean load)
+    static constexpr int CH = NS <= 16 ? 96 : 64;
     static constexpr int TT = 16;                   // timesteps per staged tile
-    static constexpr int MINB = NS <= 16 ? 6 : 1;  // 6 x 128 threads: one wave at config 4
+    static constexpr int MINB = NS <= 16 ? 8 : 1;
 };
 
 template <typename T, int NS, bool HAS_Z, bool CARRY>
