@@ -179,9 +179,15 @@ def _cpu_scan_seconds(dim_s):
 
 
 def _cpu_sample_dim(budget_s):
+    """Channels of a CPU sample that takes about `budget_s`: a warmed-up probe, then one
+    refinement (the oracle's time is not linear in the channel count: per-step overheads at
+    small counts, cache spills at large ones)."""
     probe = 8
+    _cpu_scan_seconds(probe)  # warm-up
     tp = _cpu_scan_seconds(probe)
-    return int(max(probe, min(CFG["dim"], probe * budget_s / max(tp, 1e-3))))
+    dim_s = int(max(probe, min(CFG["dim"], probe * budget_s / max(tp, 1e-3))))
+    t1 = _cpu_scan_seconds(dim_s)
+    return int(max(probe, min(CFG["dim"], dim_s * budget_s / max(t1, 1e-3))))
 
 
 def _cpu_record(dim_s, dt):
