@@ -156,6 +156,30 @@ def _rms_along(t, weight, eps, dim):
     return y.to(t.dtype).contiguous()
 
 
+def selective_scan_full_matrix_cuda(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softplus=False,
+                                   return_last_state=False, P=None, Q=None, gamma=None):
+    """The reference's full-matrix P/Q entry point (``selective_scan_interface.py:262-350``):
+    same arguments, checks and results, computed by the P/Q kernels instead of a per-step
+    torch loop (gradients included, ``gamma`` unused as there)."""
+    if P is None or Q is None:
+        raise ValueError("P and Q must both be provided for full-matrix path")
+    if A.is_complex():
+        raise NotImplementedError("Full-matrix P/Q path currently supports real A only")
+    if not all(t.is_cuda for t in (u, delta, A, B, C, P, Q)):
+        raise ValueError("Full-matrix path requires CUDA tensors")
+    return SelectiveScanPQFn.apply(u, delta, A, B, C, D, z, delta_bias, delta_softplus, return_last_state, P, Q,
+                                   gamma)
+
+
+def rms_norm_forward(x, weight, bias, eps=1e-6, is_rms_norm=True):
+    """The reference's helper (``selective_scan_interface.py:217-234``): normalises the last
+    dimension of x (no autograd through it, as there)."""
+    from .layer_norm import _layer_norm_fwd
+    x = x if x.stride(-1) == 1 else x.contiguous()
+    return _layer_norm_fwd(x, weight.contiguous(), bias.contiguous() if bias is not None else None, eps, None,
+                           residual_dtype=None, is_rms_norm=is_rms_norm)[0]
+
+
 class MambaInnerFn(torch.autograd.Function):
 
     @staticmethod

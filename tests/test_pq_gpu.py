@@ -144,3 +144,25 @@ def test_pq_partial_tile_repeatable():
                 assert_close(grads[k], runs[0][2][k], 1e-6, 1e-6, k)
             else:
                 assert torch.equal(grads[k], runs[0][2][k]), k
+
+
+def test_full_matrix_entry_point_equals_selective_scan_fn():
+    """selective_scan_full_matrix_cuda (the reference's per-step P/Q path, here on the kernels)
+    gives selective_scan_fn's P/Q results and gradients; its argument checks raise as there."""
+    from motif_ssm.selective_scan_interface import selective_scan_full_matrix_cuda
+    from motif_ssm import selective_scan_fn
+    inp, dout = make_scan_inputs(2, 24, 150, 16, torch.float32, seed=21, pq_rank=2)
+    res = []
+    for fn in (selective_scan_full_matrix_cuda, selective_scan_fn):
+        leaves = {k: v.to(DEV).clone().requires_grad_(True) for k, v in inp.items() if v is not None}
+        out, last = fn(leaves["u"], leaves["delta"], leaves["A"], leaves["B"], leaves["C"], leaves["D"],
+                       z=leaves["z"], delta_bias=leaves["delta_bias"], delta_softplus=True, return_last_state=True,
+                       P=leaves["P"], Q=leaves["Q"])
+        out.backward(dout.to(DEV))
+        res.append((out, last, {k: v.grad for k, v in leaves.items()}))
+    assert torch.equal(res[0][0], res[1][0]) and torch.equal(res[0][1], res[1][1])
+    for k in res[0][2]:
+        assert_close(res[0][2][k], res[1][2][k], 1e-6, 1e-6, k)
+    with pytest.raises(ValueError):
+        selective_scan_full_matrix_cuda(res[0][0], res[0][0], inp["A"].to(DEV), inp["B"].to(DEV),
+                                        inp["C"].to(DEV), P=None, Q=inp["Q"].to(DEV))
