@@ -233,6 +233,30 @@ MSS_API int64_t add_rms_norm_args_size(void);
  * followed by selective_state_update, mamba_simplemotif.py:363-399); a->dt is not read. */
 MSS_API int ssm_state_update_dtproj(const ssm_state_update_args *a, const ssm_dtproj_args *p, void *stream);
 
+/* Motif regulariser over a batch of cc x cc fp32 matrices (the P_eff @ Q squares of the
+ * coupled layers; replaces motifRegular.cal, motif/train_kpq_motif_pile_lm.py:405-466, one
+ * matrix per call there).  Per matrix: soft edges w = sigmoid(amplitude (a^2 - bias)) off the
+ * diagonal, the 13 three-node motif densities obs[1..13] (obs[0] = 0) divided by
+ * cc (cc-1) (cc-2) / 6, and loss = sum over i with target[i] > 0 of weight[i] diff_i^2,
+ * diff_i = obs[i+1] - target[i] (log_mse: log(max(obs, eps)) - log(max(target, eps))).
+ * With dloss given, also da = dloss * d loss / d a.  3 <= cc <= 32; rows unit stride. */
+typedef struct {
+    int64_t n_mat, cc;
+    const float *a;       int64_t a_ms;        /* (n_mat, cc, cc): matrix stride, row stride cc */
+    const float *target;                       /* (13,) on the device; <= 0 entries are skipped */
+    const float *weight;                       /* nullable (13,) on the device: all ones */
+    float amplitude, bias;
+    int32_t log_mse;      float log_eps;
+    float *loss;                               /* (n_mat,) */
+    float *obs;                                /* nullable (n_mat, 14) */
+    const float *dloss;                        /* nullable (n_mat,): when given, da is written */
+    float *da;            int64_t da_ms;       /* (n_mat, cc, cc) */
+} motif_regular_args;
+
+MSS_API int motif_regular(const motif_regular_args *a, void *stream);
+/* sizeof(motif_regular_args), for binding-side layout checks. */
+MSS_API int64_t motif_regular_args_size(void);
+
 /* Message of the last failure on the calling thread ("" if none). */
 MSS_API const char *ss_last_error(void);
 /* Library version string. */

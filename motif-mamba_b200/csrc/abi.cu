@@ -445,4 +445,21 @@ int add_rms_norm(const add_rms_norm_args *a, void *stream) {
     return e == cudaSuccess ? MSS_OK : cuda_fail(e, "add_rms_norm launch");
 }
 
+int64_t motif_regular_args_size(void) { return (int64_t)sizeof(motif_regular_args); }
+
+int motif_regular(const motif_regular_args *a, void *stream) {
+    if (!a) return fail(MSS_ERR_INVALID, "motif_regular: null argument struct");
+    if (a->n_mat < 0) return fail(MSS_ERR_INVALID, "motif_regular: negative n_mat");
+    if (a->cc < 3 || a->cc > 32) return fail(MSS_ERR_UNSUPPORTED, "motif_regular: cc must be in [3, 32]");
+    if (a->n_mat > 0x7fffffff) return fail(MSS_ERR_UNSUPPORTED, "motif_regular: n_mat too large");
+    if (a->n_mat == 0) return MSS_OK;
+    if (!a->a || !a->target || !a->loss) return fail(MSS_ERR_INVALID, "motif_regular: a, target and loss must be non-null");
+    if (a->a_ms < a->cc * a->cc) return fail(MSS_ERR_INVALID, "motif_regular: matrix stride below cc * cc");
+    if (a->dloss && (!a->da || a->da_ms < a->cc * a->cc))
+        return fail(MSS_ERR_INVALID, "motif_regular: da (stride >= cc * cc) is required with dloss");
+    if (a->log_mse && !(a->log_eps > 0.f)) return fail(MSS_ERR_INVALID, "motif_regular: log_eps must be > 0");
+    cudaError_t e = launch_motif_regular(*a, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? MSS_OK : cuda_fail(e, "motif_regular launch");
+}
+
 }  // extern "C"

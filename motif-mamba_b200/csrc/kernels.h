@@ -68,6 +68,7 @@ cudaError_t launch_conv1d_bwd(const conv1d_args &a, bool vec, cudaStream_t st);
 cudaError_t launch_conv1d_update(const conv1d_update_args &a, cudaStream_t st);
 cudaError_t launch_state_update(const ssm_state_update_args &a, const ssm_dtproj_args *dp, cudaStream_t st);
 cudaError_t launch_add_rms_norm(const add_rms_norm_args &a, cudaStream_t st);
+cudaError_t launch_motif_regular(const motif_regular_args &a, cudaStream_t st);
 cudaError_t launch_ss_fwd_pq(const FwdParams &p, int itype, bool has_z, cudaStream_t st);
 cudaError_t launch_ss_bwd_pq(const BwdParams &p, int itype, bool has_z, cudaStream_t st);
 cudaError_t launch_acc_to_out(const float *acc, int64_t lpitch, void *out, int itype, int64_t rows,

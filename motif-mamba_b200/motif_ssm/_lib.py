@@ -124,6 +124,18 @@ class AddRmsNormArgs(ctypes.Structure):
     ]
 
 
+class MotifRegularArgs(ctypes.Structure):
+    _fields_ = [
+        ("n_mat", i64), ("cc", i64),
+        ("a", vp), ("a_ms", i64),
+        ("target", vp), ("weight", vp),
+        ("amplitude", ctypes.c_float), ("bias", ctypes.c_float),
+        ("log_mse", i32), ("log_eps", ctypes.c_float),
+        ("loss", vp), ("obs", vp), ("dloss", vp),
+        ("da", vp), ("da_ms", i64),
+    ]
+
+
 class DtProjArgs(ctypes.Structure):
     _fields_ = [("dt_in", vp), ("dt_in_bs", i64), ("weight", vp), ("rank", i64)]
 
@@ -146,6 +158,8 @@ SYMBOLS = [
     ("ssm_state_update_dtproj", [ctypes.POINTER(StateUpdateArgs), ctypes.POINTER(DtProjArgs), vp], ctypes.c_int),
     ("add_rms_norm", [ctypes.POINTER(AddRmsNormArgs), vp], ctypes.c_int),
     ("add_rms_norm_args_size", [], i64),
+    ("motif_regular", [ctypes.POINTER(MotifRegularArgs), vp], ctypes.c_int),
+    ("motif_regular_args_size", [], i64),
     ("ss_last_error", [], ctypes.c_char_p),
     ("ss_version", [], ctypes.c_char_p),
     ("ss_abi_struct_sizes", [ctypes.POINTER(i64)], None),
@@ -176,6 +190,8 @@ def check_layout():
             raise ImportError(f"motif_ssm: {st.__name__} is {ctypes.sizeof(st)} bytes in Python but {s} in the library")
     if lib.add_rms_norm_args_size() != ctypes.sizeof(AddRmsNormArgs):
         raise ImportError("motif_ssm: AddRmsNormArgs does not match add_rms_norm_args in the library")
+    if lib.motif_regular_args_size() != ctypes.sizeof(MotifRegularArgs):
+        raise ImportError("motif_ssm: MotifRegularArgs does not match motif_regular_args in the library")
 
 
 check_layout()

@@ -212,6 +212,43 @@ def module_case(msm, name, *, batch=2, d_model=16, d_state=8, prefill=12, steps=
     print("wrote module", name)
 
 
+def load_motif_reference():
+    """The reference's ``motifRegular`` class and ``compute_model_motif_loss`` function, taken
+    out of its training script (``motif/train_kpq_motif_pile_lm.py:405-466, 590-642``) by
+    ``ast`` and executed alone: the script's other top-level code (argument parsing, data,
+    distributed setup) is not run."""
+    import ast
+    path = os.path.join(REF, "motif/train_kpq_motif_pile_lm.py")
+    src = open(path).read()
+    tree = ast.parse(src)
+    keep = [n for n in tree.body if getattr(n, "name", None) in ("motifRegular", "compute_model_motif_loss")]
+    assert len(keep) == 2, "motifRegular / compute_model_motif_loss not found"
+    ns = {"torch": torch}
+    exec(compile(ast.Module(body=keep, type_ignores=[]), path, "exec"), ns)
+    return ns
+
+
+def motif_case(ns, name, *, n_mat, cc, scale, amplitude, bias, fre, loss_form="mse", loss_weights=None,
+               seed=0):
+    """Loss, densities and d loss / d a of the reference's motifRegular.cal, matrix by matrix."""
+    g = torch.Generator().manual_seed(seed)
+    mats = scale * torch.randn(n_mat, cc, cc, generator=g)
+    reg = ns["motifRegular"](fre, device="cpu", cc=cc, loss_form=loss_form, loss_weights=loss_weights)
+    losses, obs, grads = [], [], []
+    for i in range(n_mat):
+        a = mats[i].clone().requires_grad_(True)
+        r, o = reg.cal(a, amplitude=amplitude, bias=bias)
+        r.backward()
+        losses.append(r.detach().clone())
+        obs.append(o.detach().clone())
+        grads.append(a.grad.detach().clone())
+    rec = dict(name=name, kind="motif", mats=mats, cc=cc, amplitude=amplitude, bias=bias,
+               fre=torch.tensor(fre, dtype=torch.float32), loss_form=loss_form, loss_weights=loss_weights,
+               loss=torch.stack(losses), obs=torch.stack(obs), grad=torch.stack(grads))
+    torch.save(rec, os.path.join(HERE, f"motif_{name}.pt"))
+    print("wrote motif", name, n_mat, cc)
+
+
 def main():
     torch.set_num_threads(min(8, os.cpu_count() or 1))
     ssi, msm = load_reference()
@@ -231,6 +268,17 @@ def main():
     module_case(msm, "small")
     module_case(msm, "pq2", pq_rank=2, seed=3, pq_k=40.0)
     module_case(msm, "pq3_perdim", d_state=16, pq_rank=3, pq_per_dim=True, seed=4)
+    ns = load_motif_reference()
+    mavgf = [0.0455015, 0.1438295, 0.0891085, 0.053934, -1, -1, -1, -1, -1, -1, 0.065183, 0.1245175, 0.0]
+    single2 = [-1.0] * 13
+    single2[1] = 0.25  # --motif-class 2, the script's default
+    # the script's default amplitude / bias, matrices around the threshold sqrt(bias)
+    motif_case(ns, "default_class2", n_mat=6, cc=16, scale=0.01, amplitude=1e5, bias=5e-5, fre=single2, seed=11)
+    motif_case(ns, "mavgf_weighted", n_mat=5, cc=16, scale=0.01, amplitude=1e5, bias=5e-5, fre=mavgf,
+               loss_weights=[1.0, 2.0, 0.5, 1.0, 1, 1, 1, 1, 1, 1, 3.0, 0.25, 1], seed=12)
+    motif_case(ns, "log_mse_cc8", n_mat=4, cc=8, scale=1.0, amplitude=4.0, bias=0.5, fre=mavgf,
+               loss_form="log_mse", seed=13)
+    motif_case(ns, "soft_cc32", n_mat=2, cc=32, scale=1.0, amplitude=2.0, bias=0.8, fre=mavgf, seed=14)
 
 
 if __name__ == "__main__":

@@ -122,3 +122,21 @@ def test_python_shim_raises_on_unbuilt_paths():
         selective_scan_fn(u, u, torch.complex(A, A), B, B, P=torch.zeros(4, 2), Q=torch.zeros(2, 4))
     with pytest.raises(ValueError):               # P without Q
         selective_scan_fn(u, u, A, B, B, P=torch.zeros(4, 2))
+
+
+def test_motif_regular_validates_before_launch():
+    a = _lib.MotifRegularArgs()
+    a.n_mat, a.cc = 1, 33
+    assert _lib.lib.motif_regular(ctypes.byref(a), None) == _lib.MSS_ERR_UNSUPPORTED
+    a.cc = 16
+    assert _lib.lib.motif_regular(ctypes.byref(a), None) == _lib.MSS_ERR_INVALID  # null pointers
+    a.n_mat = 0
+    assert _lib.lib.motif_regular(ctypes.byref(a), None) == 0  # empty batch: no-op
+    import torch
+    from motif_ssm.motif_regular import motifRegular
+    reg = motifRegular([0.25] * 13, device="cpu")
+    assert reg.sum == 560 and reg.P.sum().item() == 16 * 15
+    with pytest.raises(RuntimeError):  # no CPU path
+        reg.cal(torch.zeros(16, 16), amplitude=1e5, bias=5e-5)
+    with pytest.raises(ValueError):
+        motifRegular([0.25] * 13, device="cpu", loss_weights=[1.0] * 12)

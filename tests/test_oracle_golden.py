@@ -103,3 +103,20 @@ def test_module_pq_oracle_matches_reference(name):
         torch.testing.assert_close(o, rec["step_out"][i], rtol=1e-5, atol=1e-5)
     torch.testing.assert_close(conv_state, rec["conv_state_final"])
     torch.testing.assert_close(ssm_state, rec["ssm_state_final"], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(GOLD, "motif_*.pt"))),
+                         ids=lambda p: os.path.basename(p))
+def test_motif_oracle_matches_reference(path):
+    """motif_regular_ref reproduces the reference's motifRegular.cal: loss, densities, d loss / d a."""
+    from oracle import motif_oracle as MO
+    rec = _load(path)
+    for i in range(rec["mats"].shape[0]):
+        a = rec["mats"][i].clone().requires_grad_(True)
+        r, obs = MO.motif_regular_ref(a, rec["fre"], rec["amplitude"], rec["bias"], rec["loss_form"],
+                                      loss_weights=rec["loss_weights"])
+        r.backward()
+        torch.testing.assert_close(r.detach(), rec["loss"][i], rtol=1e-5, atol=1e-7)
+        torch.testing.assert_close(obs, rec["obs"][i], rtol=1e-5, atol=1e-7)
+        g = rec["grad"][i]
+        torch.testing.assert_close(a.grad, g, rtol=1e-4, atol=1e-5 * (g.abs().max().item() + 1e-9))
