@@ -452,14 +452,12 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
                             S1[m] = fma2(dh2[s][m], Bv[s][m], S1[m]);
                             S2[m] = fma2(Anp[s], gv, S2[m]);
                             dA2[s] = fma2(dtf2[m], gv, dA2[s]);
-                            const f32x2 pb = mul2(dh2[s][m], dtu2[m]);
-                            const f32x2 pc = mul2(dog2[m], h2[s][m]);
                             if (mm == 0) {
-                                vb.x = add2(vb.x, pb);
-                                vc.x = add2(vc.x, pc);
+                                vb.x = fma2(dh2[s][m], dtu2[m], vb.x);
+                                vc.x = fma2(dog2[m], h2[s][m], vc.x);
                             } else {
-                                vb.y = add2(vb.y, pb);
-                                vc.y = add2(vc.y, pc);
+                                vb.y = fma2(dh2[s][m], dtu2[m], vb.y);
+                                vc.y = fma2(dog2[m], h2[s][m], vc.y);
                             }
                         }
                         if (live) {
