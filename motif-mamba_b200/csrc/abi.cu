@@ -16,7 +16,6 @@ using namespace mss;
 namespace {
 
 thread_local std::string g_err;
-constexpr int kNumSMs = 148;  // B200
 
 int fail(int code, const char *fmt, ...) __attribute__((format(printf, 2, 3)));
 int fail(int code, const char *fmt, ...) {
@@ -46,9 +45,9 @@ FwdShape fwd_shape(const ss_fwd_args *a) {
     FwdShape s{1, (int)a->seqlen, 0, 0};
     const int64_t rows = a->batch * a->dim;
     // Few rows (small batch x channels): split the sequence into segments so that rows x
-    // segments fills up to one wave of resident threads (6 CTAs of 128 per SM for dstate <= 16);
-    // segments are whole 16-step tiles.  A carry pass gives every segment its initial state.
-    const int64_t capacity = (int64_t)kNumSMs * (a->dstate <= 16 ? 768 : 128);
+    // segments fills up to one wave of resident rows; segments are whole 16-step tiles.  A
+    // carry pass gives every segment its initial state.
+    const int64_t capacity = (int64_t)kNumSMs * fwd_rows_per_sm((int)a->dstate, rows);
     const int64_t n_want = rows > 0 ? capacity / rows : 1;
     if (!a->P && rows > 0 && n_want >= 2 && a->seqlen >= 4 * 64) {
         // at most 16 segments (every segment folds the carries of the earlier ones) of >= 64 steps

@@ -57,6 +57,8 @@ struct BwdParams {
 int set_last_error(int code, const char *msg);
 
 int fwd_state_pad(int dstate);
+// resident rows per SM of the forward variant chosen for batch x dim = rows
+int fwd_rows_per_sm(int dstate, int64_t rows);
 int fwd_channels_per_cta(int dstate);
 cudaError_t launch_ss_fwd(const FwdParams &p, int itype, bool has_z, cudaStream_t st);
 

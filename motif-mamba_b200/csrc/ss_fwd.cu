@@ -30,19 +30,57 @@
 
 namespace mss {
 
-template <int NS> struct FwdCfg {
-    // channels (threads) per CTA: 96 x 8 resident CTAs per SM; at config 4 the 1024 CTAs
-    // spread as 6 or 7 per SM (128-channel CTAs would leave 5 or 6, the SMs with 6 setting the
-    // pace at 86 % of the mean load)
-    static constexpr int CH = NS <= 16 ? 96 : 64;
-    static constexpr int TT = 16;                   // timesteps per staged tile
-    static constexpr int MINB = NS <= 16 ? 8 : 1;
+int fwd_state_pad(int dstate) {
+    if (dstate <= 4) return 4;
+    if (dstate <= 8) return 8;
+    if (dstate <= 16) return 16;
+    if (dstate <= 32) return 32;
+    return 64;
+}
+
+template <int NS, int SPT> struct FwdCfg {
+    // SPT states per thread: a row with more states than that is split over LPC adjacent
+    // lanes, and y = <C, h> is summed over the row's lanes by shuffles.  Splitting multiplies
+    // the per-step work that does not depend on the state (dt, softplus, the decay base) by
+    // LPC, so it pays only when rows are few: dstate 32 / 64 runs whole rows per thread when
+    // there are at least a wave of them and halves otherwise (fwd_spt).
+    static_assert(NS % SPT == 0, "whole lanes per row");
+    static constexpr int LPC = NS / SPT;  // threads (lanes) per row
+    // threads per CTA: for dstate <= 16, 96 x 8 resident CTAs per SM; at config 4 the 1024
+    // CTAs spread as 6 or 7 per SM (128-channel CTAs would leave 5 or 6, the SMs with 6
+    // setting the pace at 86 % of the mean load)
+    static constexpr int NT = NS <= 16 ? 96 : 128;
+    static constexpr int CH = NT / LPC;   // channels (rows) per CTA
+    static constexpr int TT = 16;         // timesteps per staged tile
+    // resident CTAs per SM: registers per thread grow with SPT (~80 at 16, ~170 at 32 split
+    // in two, ~250 for 32 or 64 states in one thread)
+    static constexpr int MINB = NS <= 16 ? 8 : (SPT == 16 ? 4 : (LPC == 1 ? 2 : 3));
 };
 
-template <typename T, int NS, bool HAS_Z, bool CARRY>
+// Resident rows per SM of the variant fwd_spt picks (sizes the time split).
+static int rows_per_sm(int ns, int spt) {
+    if (ns <= 16) return 768;
+    const int lpc = ns / spt, minb = spt == 16 ? 4 : (lpc == 1 ? 2 : 3);
+    return minb * 128 / lpc;
+}
+
+int fwd_spt(int ns, int64_t rows) {
+    if (ns <= 16) return ns;
+    const int whole = ns;           // one thread per row
+    const int half = ns / 2;        // two threads per row
+    return rows >= (int64_t)kNumSMs * rows_per_sm(ns, whole) ? whole : half;
+}
+
+int fwd_rows_per_sm(int dstate, int64_t rows) {
+    const int ns = fwd_state_pad(dstate);
+    return rows_per_sm(ns, fwd_spt(ns, rows));
+}
+
+template <typename T, int NS, int SPT, bool HAS_Z, bool CARRY>
 struct FwdLayout {
-    static constexpr int CH = FwdCfg<NS>::CH;
-    static constexpr int TT = FwdCfg<NS>::TT;
+    static constexpr int CH = FwdCfg<NS, SPT>::CH;
+    static constexpr int NT = FwdCfg<NS, SPT>::NT;
+    static constexpr int TT = FwdCfg<NS, SPT>::TT;
     static constexpr int RP = TT * (int)sizeof(T) + 16;  // padded row pitch (conflict-free 16-B reads)
     static constexpr int NCH_ARR = CARRY ? 2 : (HAS_Z ? 3 : 2);  // u, delta, (z)
     static constexpr int NST_ARR = CARRY ? 1 : 2;                // B, (C)
@@ -54,14 +92,17 @@ struct FwdLayout {
     static constexpr int SMEM = BUF + TT * BCW * 4;  // single-buffered: co-resident CTAs hide the loads
 };
 
-template <typename T, int NS, bool HAS_Z, bool CARRY>
-__global__ void __launch_bounds__(FwdCfg<NS>::CH, FwdCfg<NS>::MINB) ss_fwd_kernel(const FwdParams p) {
-    using Ly = FwdLayout<T, NS, HAS_Z, CARRY>;
-    constexpr int CH = Ly::CH, TT = Ly::TT, RP = Ly::RP, BCW = Ly::BCW;
+template <typename T, int NS, int SPT, bool HAS_Z, bool CARRY>
+__global__ void __launch_bounds__(FwdCfg<NS, SPT>::NT, FwdCfg<NS, SPT>::MINB) ss_fwd_kernel(const FwdParams p) {
+    using Ly = FwdLayout<T, NS, SPT, HAS_Z, CARRY>;
+    constexpr int CH = Ly::CH, NT = Ly::NT, TT = Ly::TT, RP = Ly::RP, BCW = Ly::BCW;
+    constexpr int LPC = FwdCfg<NS, SPT>::LPC;
     extern __shared__ __align__(16) char smem[];
     float *bc = reinterpret_cast<float *>(smem + Ly::BUF);
 
     const int tid = threadIdx.x;
+    const int ch = tid / LPC;                  // this thread's row within the CTA
+    const int n0 = (tid - ch * LPC) * SPT;     // and its first state
     const int g = blockIdx.x / p.tiles_per_group;
     const int tile = blockIdx.x - g * p.tiles_per_group;
     const int s = blockIdx.y;
@@ -69,22 +110,23 @@ __global__ void __launch_bounds__(FwdCfg<NS>::CH, FwdCfg<NS>::MINB) ss_fwd_kerne
     const int cg0 = tile * CH;                 // first channel of this CTA within its group
     const int c0 = g * p.dpg + cg0;            // first channel overall
     const int nvalid_ch = min(CH, p.dpg - cg0);
-    const bool valid = tid < nvalid_ch;
-    const int d = c0 + (valid ? tid : 0);
+    const bool valid = ch < nvalid_ch;
+    const int d = c0 + (valid ? ch : 0);
     const int64_t L = p.seqlen;
     const int64_t t_begin = (int64_t)s * p.seg_len;
     const int64_t t_end = min(L, t_begin + (int64_t)p.seg_len);
     const bool aligned = p.aligned != 0;
 
-    float A2[NS];
+    float A2[SPT];  // rates of states n0 .. n0 + SPT - 1 (times log2 e)
 #pragma unroll
-    for (int n = 0; n < NS; ++n)
-        A2[n] = (valid && n < p.dstate) ? p.A[(int64_t)d * p.A_ds + (int64_t)n * p.A_ns] * kLog2e : 0.f;
+    for (int j = 0; j < SPT; ++j)
+        A2[j] = (valid && n0 + j < p.dstate) ? p.A[(int64_t)d * p.A_ds + (int64_t)(n0 + j) * p.A_ns] * kLog2e : 0.f;
+    const float A2r = LPC == 1 ? A2[0] : (valid ? p.A[(int64_t)d * p.A_ds] * kLog2e : 0.f);  // state 0's rate
     const float Dv = (p.D != nullptr && valid) ? p.D[(int64_t)d * p.D_s] : 0.f;
     const float bias = (p.delta_bias != nullptr && valid) ? p.delta_bias[(int64_t)d * p.delta_bias_s] : 0.f;
 
     // State and decay rates as packed pairs (states 2m, 2m+1).
-    constexpr int NP = NS / 2;
+    constexpr int NP = SPT / 2;
     f32x2 h2[NP], A2p[NP];
 #pragma unroll
     for (int m = 0; m < NP; ++m) {
@@ -96,10 +138,11 @@ __global__ void __launch_bounds__(FwdCfg<NS>::CH, FwdCfg<NS>::MINB) ss_fwd_kerne
     // of one per state.  Checked per channel to 1e-6 relative (the -exp(log(n+1)) round trip
     // of the module's A_log deviates by < 2e-7); a CTA takes the chained path only if all its
     // channels qualify, otherwise every state gets its own ex2.
-    bool chain_ok = A2[0] != 0.f || !valid;
+    bool chain_ok = A2r != 0.f || !valid;
 #pragma unroll
-    for (int n = 1; n < NS; ++n)
-        if (n < p.dstate) chain_ok = chain_ok && fabsf(A2[n] - (float)(n + 1) * A2[0]) <= 1e-6f * fabsf(A2[n]);
+    for (int j = 0; j < SPT; ++j)
+        if (n0 + j > 0 && n0 + j < p.dstate)
+            chain_ok = chain_ok && fabsf(A2[j] - (float)(n0 + j + 1) * A2r) <= 1e-6f * fabsf(A2[j]);
     const bool chain = __syncthreads_and(chain_ok) != 0;
     float cum = 0.f;  // sum of dt since t = 0 (main pass) or since the segment start (carry pass)
     const int64_t row = (int64_t)b * p.dim + d;
@@ -107,10 +150,10 @@ __global__ void __launch_bounds__(FwdCfg<NS>::CH, FwdCfg<NS>::MINB) ss_fwd_kerne
         // fold the carries of the earlier segments: h = decay(segment) h + H(segment)
         for (int sp = 0; sp < s; ++sp) {
             const float dts = p.ws_dts[row * p.n_seg + sp];
-            const float *H = p.ws_h + (row * p.n_seg + sp) * NS;
+            const float *H = p.ws_h + (row * p.n_seg + sp) * NS + n0;
             if (chain) {  // decay of state n over the segment = R^(n+1), R = exp(A_0 dts)
-                const float R = ex2(A2[0] * dts);
-                float pw = R;
+                const float R = ex2(A2r * dts);
+                float pw = LPC == 1 ? R : ex2(A2[0] * dts);  // R^(n0 + 1)
 #pragma unroll
                 for (int m = 0; m < NP; ++m) {
                     const float2 hv = unpack2(h2[m]);
@@ -139,13 +182,13 @@ __global__ void __launch_bounds__(FwdCfg<NS>::CH, FwdCfg<NS>::MINB) ss_fwd_kerne
     auto stage = [&](int buf, int64_t t0) {
         char *rb = smem + buf * Ly::BUF;
         const int tv = (int)min((int64_t)TT, t_end - t0);
-        stage_tile<T, TT>(rb + Ly::U_OFF, RP, gu, p.u_ds, CH, nvalid_ch, t0, tv, aligned, tid, CH);
-        stage_tile<T, TT>(rb + Ly::DT_OFF, RP, gdt, p.delta_ds, CH, nvalid_ch, t0, tv, aligned, tid, CH);
+        stage_tile<T, TT>(rb + Ly::U_OFF, RP, gu, p.u_ds, CH, nvalid_ch, t0, tv, aligned, tid, NT);
+        stage_tile<T, TT>(rb + Ly::DT_OFF, RP, gdt, p.delta_ds, CH, nvalid_ch, t0, tv, aligned, tid, NT);
         if constexpr (HAS_Z && !CARRY)
-            stage_tile<T, TT>(rb + Ly::Z_OFF, RP, gz, p.z_ds, CH, nvalid_ch, t0, tv, aligned, tid, CH);
-        stage_tile<T, TT>(rb + Ly::B_OFF, RP, gB, p.B_ns, NS, p.dstate, t0, tv, aligned, tid, CH);
+            stage_tile<T, TT>(rb + Ly::Z_OFF, RP, gz, p.z_ds, CH, nvalid_ch, t0, tv, aligned, tid, NT);
+        stage_tile<T, TT>(rb + Ly::B_OFF, RP, gB, p.B_ns, NS, p.dstate, t0, tv, aligned, tid, NT);
         if constexpr (!CARRY)
-            stage_tile<T, TT>(rb + Ly::C_OFF, RP, gC, p.C_ns, NS, p.dstate, t0, tv, aligned, tid, CH);
+            stage_tile<T, TT>(rb + Ly::C_OFF, RP, gC, p.C_ns, NS, p.dstate, t0, tv, aligned, tid, NT);
     };
 
     const int ntiles = (int)((t_end - t_begin + TT - 1) / TT);
@@ -158,7 +201,7 @@ __global__ void __launch_bounds__(FwdCfg<NS>::CH, FwdCfg<NS>::MINB) ss_fwd_kerne
         __syncthreads();
         char *rb = smem;
         // B / C tile -> fp32 [t][n] (C after B), once per CTA.
-        for (int i = tid; i < TT * NS; i += CH) {
+        for (int i = tid; i < TT * NS; i += NT) {
             const int n = i % NS, t = i / NS;
             bc[t * BCW + n] = to_f<T>(reinterpret_cast<const T *>(rb + Ly::B_OFF + n * RP)[t]);
             if constexpr (!CARRY)
@@ -166,8 +209,8 @@ __global__ void __launch_bounds__(FwdCfg<NS>::CH, FwdCfg<NS>::MINB) ss_fwd_kerne
         }
         __syncthreads();
 
-        T *ur = reinterpret_cast<T *>(rb + Ly::U_OFF + tid * RP);
-        const T *dr = reinterpret_cast<const T *>(rb + Ly::DT_OFF + tid * RP);
+        T *ur = reinterpret_cast<T *>(rb + Ly::U_OFF + ch * RP);
+        const T *dr = reinterpret_cast<const T *>(rb + Ly::DT_OFF + ch * RP);
 #pragma unroll 1
         for (int g8 = 0; g8 < TT; g8 += 8) {
             float uf[8], dv[8], dtu[8];
@@ -186,14 +229,16 @@ __global__ void __launch_bounds__(FwdCfg<NS>::CH, FwdCfg<NS>::MINB) ss_fwd_kerne
             auto steps = [&](auto chained) {
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
-                    const f32x2 *bcr = reinterpret_cast<const f32x2 *>(bc + (g8 + j) * BCW);
+                    const f32x2 *bcr = reinterpret_cast<const f32x2 *>(bc + (g8 + j) * BCW + n0);  // B[n0..]
+                    const f32x2 *ccr = reinterpret_cast<const f32x2 *>(bc + (g8 + j) * BCW + NS + n0);  // C[n0..]
                     const f32x2 du2 = pack2(dtu[j], dtu[j]);
                     f32x2 acc2[2] = {pack2(0.f, 0.f), pack2(0.f, 0.f)};  // two chains of pair sums
                     f32x2 ap, q;  // chained path: (r^(2m+1), r^(2m+2)) and the step (r^2, r^2)
                     if constexpr (decltype(chained)::value) {
-                        const float r = ex2(dv[j] * A2[0]);
+                        const float r = ex2(dv[j] * A2r);
                         const float r2 = r * r;
-                        ap = pack2(r, r2);
+                        const float rs = LPC == 1 ? r : ex2(dv[j] * A2[0]);  // r^(n0 + 1)
+                        ap = pack2(rs, rs * r);
                         q = pack2(r2, r2);
                     }
                     const f32x2 dt2 = pack2(dv[j], dv[j]);
@@ -207,7 +252,7 @@ __global__ void __launch_bounds__(FwdCfg<NS>::CH, FwdCfg<NS>::MINB) ss_fwd_kerne
                             a2 = ex2x2(mul2(dt2, A2p[m]));
                         }
                         h2[m] = fma2(a2, h2[m], mul2(du2, bcr[m]));
-                        if constexpr (!CARRY) acc2[m & 1] = fma2(bcr[NP + m], h2[m], acc2[m & 1]);
+                        if constexpr (!CARRY) acc2[m & 1] = fma2(ccr[m], h2[m], acc2[m & 1]);
                     }
                     const float2 accv = unpack2(add2(acc2[0], acc2[1]));
                     y[j] = accv.x + accv.y;
@@ -218,17 +263,25 @@ __global__ void __launch_bounds__(FwdCfg<NS>::CH, FwdCfg<NS>::MINB) ss_fwd_kerne
             else
                 steps(std::false_type{});
             if constexpr (!CARRY) {
+                if constexpr (LPC > 1) {  // sum the row's lanes (adjacent lanes of one warp)
+#pragma unroll
+                    for (int o = 1; o < LPC; o <<= 1)
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) y[j] += __shfl_xor_sync(0xffffffffu, y[j], o);
+                }
                 float o[8];
 #pragma unroll
                 for (int j = 0; j < 8; ++j) o[j] = fmaf(Dv, uf[j], y[j]);
-                Vec8<T>::store(ur + g8, o);  // out, in place of u
+                if (LPC == 1 || n0 == 0) Vec8<T>::store(ur + g8, o);  // out, in place of u
                 if constexpr (HAS_Z) {
-                    T *zr = reinterpret_cast<T *>(rb + Ly::Z_OFF + tid * RP);
-                    float zf[8];
-                    Vec8<T>::load(zr + g8, zf);
+                    if (LPC == 1 || n0 == 0) {
+                        T *zr = reinterpret_cast<T *>(rb + Ly::Z_OFF + ch * RP);
+                        float zf[8];
+                        Vec8<T>::load(zr + g8, zf);
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) zf[j] = o[j] * zf[j] * sigmoidf_(zf[j]);
-                    Vec8<T>::store(zr + g8, zf);  // out_z, in place of z
+                        for (int j = 0; j < 8; ++j) zf[j] = o[j] * zf[j] * sigmoidf_(zf[j]);
+                        Vec8<T>::store(zr + g8, zf);  // out_z, in place of z
+                    }
                 }
             }
         }
@@ -238,72 +291,73 @@ __global__ void __launch_bounds__(FwdCfg<NS>::CH, FwdCfg<NS>::MINB) ss_fwd_kerne
                 const int64_t k = (te - 1) / kChunkLen;
                 float *xr = p.x + (row * p.n_chunks + k) * 2 * p.dstate;
 #pragma unroll
-                for (int n = 0; n < NS; ++n)
-                    if (n < p.dstate) {
-                        xr[2 * n] = ex2(A2[n] * cum);
-                        const float2 hv = unpack2(h2[n >> 1]);
-                        xr[2 * n + 1] = (n & 1) ? hv.y : hv.x;
+                for (int j = 0; j < SPT; ++j)
+                    if (n0 + j < p.dstate) {
+                        xr[2 * (n0 + j)] = ex2(A2[j] * cum);
+                        const float2 hv = unpack2(h2[j >> 1]);
+                        xr[2 * (n0 + j) + 1] = (j & 1) ? hv.y : hv.x;
                     }
             }
             __syncthreads();
             T *go = reinterpret_cast<T *>(p.out) + (int64_t)b * p.out_bs + (int64_t)c0 * p.out_ds;
-            store_tile<T, TT>(go, p.out_ds, rb + Ly::U_OFF, RP, nvalid_ch, t0, tv, aligned, tid, CH);
+            store_tile<T, TT>(go, p.out_ds, rb + Ly::U_OFF, RP, nvalid_ch, t0, tv, aligned, tid, NT);
             if constexpr (HAS_Z) {
                 T *goz = reinterpret_cast<T *>(p.out_z) + (int64_t)b * p.out_z_bs + (int64_t)c0 * p.out_z_ds;
-                store_tile<T, TT>(goz, p.out_z_ds, rb + Ly::Z_OFF, RP, nvalid_ch, t0, tv, aligned, tid, CH);
+                store_tile<T, TT>(goz, p.out_z_ds, rb + Ly::Z_OFF, RP, nvalid_ch, t0, tv, aligned, tid, NT);
             }
         }
         __syncthreads();
     }
     if (CARRY && valid) {
-        float *H = p.ws_h + (row * p.n_seg + s) * NS;
+        float *H = p.ws_h + (row * p.n_seg + s) * NS + n0;
 #pragma unroll
         for (int m = 0; m < NP; ++m) {
             const float2 hv = unpack2(h2[m]);
             H[2 * m] = hv.x;
             H[2 * m + 1] = hv.y;
         }
-        p.ws_dts[row * p.n_seg + s] = cum;
+        if (n0 == 0) p.ws_dts[row * p.n_seg + s] = cum;
     }
 }
 
-template <typename T, int NS, bool HAS_Z, bool CARRY>
+template <typename T, int NS, int SPT, bool HAS_Z, bool CARRY>
 static cudaError_t launch_one(const FwdParams &p, dim3 grid, cudaStream_t st) {
-    using Ly = FwdLayout<T, NS, HAS_Z, CARRY>;
-    auto kern = ss_fwd_kernel<T, NS, HAS_Z, CARRY>;
+    using Ly = FwdLayout<T, NS, SPT, HAS_Z, CARRY>;
+    auto kern = ss_fwd_kernel<T, NS, SPT, HAS_Z, CARRY>;
     static std::atomic<unsigned long long> smem_set{0};
     {
         const cudaError_t e = set_smem_once(smem_set, reinterpret_cast<const void *>(kern), Ly::SMEM);
         if (e != cudaSuccess) return e;
     }
-    kern<<<grid, Ly::CH, Ly::SMEM, st>>>(p);
+    kern<<<grid, Ly::NT, Ly::SMEM, st>>>(p);
     return cudaGetLastError();
 }
 
-template <typename T, int NS>
-static cudaError_t launch_ns(FwdParams p, bool has_z, cudaStream_t st) {
-    constexpr int CH = FwdCfg<NS>::CH;
+template <typename T, int NS, int SPT>
+static cudaError_t launch_spt(FwdParams p, bool has_z, cudaStream_t st) {
+    constexpr int CH = FwdCfg<NS, SPT>::CH;
     p.tiles_per_group = (p.dpg + CH - 1) / CH;
     dim3 grid(p.tiles_per_group * p.n_groups, p.n_seg, p.batch);
     cudaError_t e = cudaSuccess;
     if (p.n_seg > 1) {
         dim3 gc(grid.x, p.n_seg - 1, grid.z);
-        e = launch_one<T, NS, false, true>(p, gc, st);
+        e = launch_one<T, NS, SPT, false, true>(p, gc, st);
         if (e != cudaSuccess) return e;
     }
-    if (has_z) return launch_one<T, NS, true, false>(p, grid, st);
-    return launch_one<T, NS, false, false>(p, grid, st);
+    if (has_z) return launch_one<T, NS, SPT, true, false>(p, grid, st);
+    return launch_one<T, NS, SPT, false, false>(p, grid, st);
 }
 
-int fwd_state_pad(int dstate) {
-    if (dstate <= 4) return 4;
-    if (dstate <= 8) return 8;
-    if (dstate <= 16) return 16;
-    if (dstate <= 32) return 32;
-    return 64;
+template <typename T, int NS>
+static cudaError_t launch_ns(const FwdParams &p, bool has_z, cudaStream_t st) {
+    if constexpr (NS <= 16) {
+        return launch_spt<T, NS, NS>(p, has_z, st);
+    } else {
+        if (fwd_spt(NS, (int64_t)p.batch * p.dim) == NS) return launch_spt<T, NS, NS>(p, has_z, st);
+        return launch_spt<T, NS, NS / 2>(p, has_z, st);
+    }
 }
 
-int fwd_channels_per_cta(int dstate) { return fwd_state_pad(dstate) <= 16 ? 128 : 64; }
 
 template <typename T>
 static cudaError_t launch_t(const FwdParams &p, bool has_z, cudaStream_t st) {

@@ -5,7 +5,8 @@ same device inputs (B200).  Test infrastructure, not a pytest module: run it dir
     python tests/ref_kernel_timing.py [--quick]
 
 Workloads: BASELINE config 4 (32 x 3072 x L, n 16, bf16 I/O, z, D, delta_bias, softplus) at
-L = 1024 and 4096 (fwd and bwd separately), and the motif P/Q path (rank 4, shared P/Q, no z
+L = 1024 and 4096 (fwd and bwd separately), the module's d_state 32 and 64 size presets at
+8 x d_inner x 2048, and the motif P/Q path (rank 4, shared P/Q, no z
 since the reference's P/Q backward has none) at sizes the reference's one-thread-per-row kernels
 (forward O(L), backward O(L^2)) finish in seconds.  Each line: CUDA-event median over the timed
 calls after warm-up on the current stream; inputs are > 126 MB L2 for config 4.  Prints one
@@ -82,11 +83,14 @@ def main():
     from motif_ssm import selective_scan_cuda as ours
     work = [("config4", 32, 3072, L, 16, torch.bfloat16, True, 0, True) for L in ((1024,) if a.quick else (1024, 4096))]
     if not a.quick:
+        # the module's larger size presets (d_state 32 / 64, mamba_simplemotif.py:32-36), z on
+        work += [("small_n32", 8, 1024, 2048, 32, torch.bfloat16, True, 0, True),
+                 ("base_n64", 8, 1536, 2048, 64, torch.bfloat16, True, 0, True)]
         work += [("pq_fwd", 8, 1536, 2048, 16, torch.bfloat16, False, 4, False),
                  ("pq_fwd_bwd", 2, 1536, 256, 16, torch.bfloat16, False, 4, True)]
     for name, b, d, l, n, dtype, z, r, do_bwd in work:
         t = _inputs(b, d, l, n, dtype, z=z, pq_rank=r)
-        iters = 10 if name == "config4" else 3
+        iters = 3 if r else 10
         of, ob = _bench(ours, t, r > 0, 3, iters, do_bwd)
         rf, rb = _bench(ref, t, r > 0, 1 if r else 3, iters, do_bwd)
         line = {"workload": name, "batch": b, "d_inner": d, "seqlen": l, "d_state": n, "dtype": str(dtype)[6:],

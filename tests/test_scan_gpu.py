@@ -79,6 +79,13 @@ CASES = [
     (2, 24, 300, 32, torch.bfloat16, 0, True, True, True, True),   # state blocks of 16
     (1, 16, 530, 64, torch.float32, 0, True, True, True, True),
     (1, 8, 90, 20, torch.float32, 2, False, True, False, True),
+    # rows split over 2 / 4 threads (dstate 32 / 64), with time split and partial channel tiles
+    (1, 70, 1100, 32, torch.bfloat16, 0, True, True, True, True),
+    (2, 33, 700, 64, torch.float32, 0, True, True, True, True),
+    (1, 40, 300, 48, torch.float16, 2, False, True, True, True),
+    # a wave of rows or more: dstate 32 / 64 rows in one thread each
+    (38, 1000, 20, 32, torch.bfloat16, 0, True, True, True, True),
+    (40, 1000, 17, 64, torch.float32, 0, False, True, True, True),
 ]
 
 
@@ -203,19 +210,26 @@ def test_scan_extreme_delta_and_z():
     compare(out, last, grads, ref_out, ref_last, ref_grads, torch.float32, "extreme delta/z")
 
 
-@pytest.mark.parametrize("dtype,seqlen", [(torch.float32, 300), (torch.bfloat16, 700), (torch.float32, 2049)])
-def test_scan_unstructured_A(dtype, seqlen):
+@pytest.mark.parametrize("dtype,seqlen,dstate", [(torch.float32, 300, 16), (torch.bfloat16, 700, 16),
+                                                 (torch.float32, 2049, 16), (torch.float32, 2049, 32),
+                                                 (torch.bfloat16, 700, 64)])
+def test_scan_unstructured_A(dtype, seqlen, dstate):
     """A without the S4D-real (n+1) A_0 structure takes the per-state exp path."""
-    inp, dout = make_scan_inputs(2, 40, seqlen, 16, dtype, seed=seqlen + 1, random_A=True)
+    inp, dout = make_scan_inputs(2, 40, seqlen, dstate, dtype, seed=seqlen + 1, random_A=True)
     ref_out, ref_last, ref_grads = oracle(inp, dout, True)
     out, last, grads = run_kernel(inp, dout, True)
     compare(out, last, grads, ref_out, ref_last, ref_grads, dtype, "random A")
 
 
-def test_scan_mixed_structure_in_one_cta():
-    """Channels with and without the structure side by side in one CTA."""
-    inp, dout = make_scan_inputs(1, 64, 400, 16, torch.float32, seed=77)
-    inp["A"][5] = -torch.exp(torch.randn(16))
+@pytest.mark.parametrize("dstate", [16, 64])
+def test_scan_mixed_structure_in_one_cta(dstate):
+    """Channels with and without the structure side by side in one CTA (with 64 states, only
+    the last of a row's four threads sees the break)."""
+    inp, dout = make_scan_inputs(1, 64, 400, dstate, torch.float32, seed=77)
+    if dstate == 16:
+        inp["A"][5] = -torch.exp(torch.randn(16))
+    else:
+        inp["A"][5, 60] *= 1.5
     ref_out, ref_last, ref_grads = oracle(inp, dout, True)
     out, last, grads = run_kernel(inp, dout, True)
     compare(out, last, grads, ref_out, ref_last, ref_grads, torch.float32, "mixed A")
