@@ -160,6 +160,10 @@ typedef struct {
     const void *z;      int64_t z_bs;                  /* nullable */
     const float *dt_bias;                              /* nullable (dim,) */
     void *out;          int64_t out_bs;
+    /* nullable (batch,) on the device: row b updates state row state_batch_indices[b]; an index
+     * < 0 (a padding slot) or >= state_batch skips the row (state untouched, out row zero) */
+    const int32_t *state_batch_indices;
+    int64_t state_batch;                               /* rows of state (used with the indices) */
 } ssm_state_update_args;
 
 /* Residual add + RMSNorm of the pre-norm stack (the fused Add -> Norm the reference runs with

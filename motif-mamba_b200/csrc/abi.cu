@@ -400,6 +400,8 @@ int ssm_state_update(const ssm_state_update_args *a, void *stream) {
     if (a->batch * a->dim == 0) return MSS_OK;
     if (!a->state || !a->x || !a->dt || !a->A || !a->B || !a->C || !a->out)
         return fail(MSS_ERR_INVALID, "ssm_state_update: state, x, dt, A, B, C and out must be non-null");
+    if (a->state_batch_indices && a->state_batch < 1)
+        return fail(MSS_ERR_INVALID, "ssm_state_update: state_batch must be given with state_batch_indices");
     cudaError_t e = launch_state_update(*a, nullptr, static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? MSS_OK : cuda_fail(e, "ssm_state_update launch");
 }
@@ -416,6 +418,8 @@ int ssm_state_update_dtproj(const ssm_state_update_args *a, const ssm_dtproj_arg
     if (a->batch * a->dim == 0) return MSS_OK;
     if (!a->state || !a->x || !p->dt_in || !p->weight || !a->A || !a->B || !a->C || !a->out)
         return fail(MSS_ERR_INVALID, "ssm_state_update_dtproj: a required pointer is null");
+    if (a->state_batch_indices && a->state_batch < 1)
+        return fail(MSS_ERR_INVALID, "ssm_state_update_dtproj: state_batch must be given with state_batch_indices");
     cudaError_t e = launch_state_update(*a, p, static_cast<cudaStream_t>(stream));
     if (e == cudaErrorInvalidValue)
         return fail(MSS_ERR_ALIGNMENT, "ssm_state_update_dtproj: rows must be unit-stride and 16-byte aligned");

@@ -6,6 +6,8 @@
 //   dt    = softplus(dt + dt_bias)                      (if dt_softplus)
 //   state = state * exp(dt * A) + dt * B * x            (in place, state dtype)
 //   out   = sum_n state[n] * C[n] + D * x,   out *= silu(z)
+// With state_batch_indices (mamba_ssm's continuous-batching argument), batch row b reads and
+// updates state row state_batch_indices[b]; a negative index marks a padding row.
 // One thread per (batch, channel) keeps its dstate states in registers (fp32 math).
 // Decode is latency bound (a few MB per layer), so the kernel is one short launch.
 #include "common.cuh"
@@ -26,6 +28,11 @@ __global__ void __launch_bounds__(128) state_update16_vec_kernel(const ssm_state
     if (i >= a.batch * a.dim) return;
     const int64_t b = i / a.dim, d = i - b * a.dim;
     const int64_t g = d / (a.dim / a.n_groups);
+    const int64_t sb = a.state_batch_indices ? (int64_t)a.state_batch_indices[b] : b;  // state row
+    if (sb < 0 || (a.state_batch_indices && sb >= a.state_batch)) {  // padding / out of range: skipped
+        reinterpret_cast<T *>(a.out)[b * a.out_bs + d] = from_f<T>(0.f);
+        return;
+    }
     const float xv = to_f<T>(reinterpret_cast<const T *>(a.x)[b * a.x_bs + d]);
     float dt;
     if constexpr (DTP) {
@@ -47,7 +54,7 @@ __global__ void __launch_bounds__(128) state_update16_vec_kernel(const ssm_state
     if (a.dt_softplus) dt = softplus20(dt);
     const T *Bp = reinterpret_cast<const T *>(a.B) + b * a.B_bs + g * a.B_gs;
     const T *Cp = reinterpret_cast<const T *>(a.C) + b * a.C_bs + g * a.C_gs;
-    ST *st = reinterpret_cast<ST *>(a.state) + b * a.st_bs + d * a.st_ds;
+    ST *st = reinterpret_cast<ST *>(a.state) + sb * a.st_bs + d * a.st_ds;
     const float *Ar = a.A + d * a.A_ds;
     float A[NS], Bv[NS], Cv[NS], sv[NS];
 #pragma unroll
@@ -100,6 +107,11 @@ __global__ void __launch_bounds__(128) state_update_kernel(const ssm_state_updat
     if (i >= a.batch * a.dim) return;
     const int64_t b = i / a.dim, d = i - b * a.dim;
     const int64_t g = d / (a.dim / a.n_groups);
+    const int64_t sb = a.state_batch_indices ? (int64_t)a.state_batch_indices[b] : b;  // state row
+    if (sb < 0 || (a.state_batch_indices && sb >= a.state_batch)) {  // padding / out of range: skipped
+        reinterpret_cast<T *>(a.out)[b * a.out_bs + d] = from_f<T>(0.f);
+        return;
+    }
     const T *X = reinterpret_cast<const T *>(a.x);
     const T *DT = reinterpret_cast<const T *>(a.dt);
     const float xv = to_f<T>(X[b * a.x_bs + d]);
@@ -108,7 +120,7 @@ __global__ void __launch_bounds__(128) state_update_kernel(const ssm_state_updat
     if (a.dt_softplus) dt = softplus20(dt);
     const T *Bp = reinterpret_cast<const T *>(a.B) + b * a.B_bs + g * a.B_gs;
     const T *Cp = reinterpret_cast<const T *>(a.C) + b * a.C_bs + g * a.C_gs;
-    ST *st = reinterpret_cast<ST *>(a.state) + b * a.st_bs + d * a.st_ds;
+    ST *st = reinterpret_cast<ST *>(a.state) + sb * a.st_bs + d * a.st_ds;
     const float dtx = dt * xv;
     float y = 0.f;
 #pragma unroll

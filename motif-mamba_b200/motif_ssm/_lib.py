@@ -107,6 +107,7 @@ class StateUpdateArgs(ctypes.Structure):
         ("z", vp), ("z_bs", i64),
         ("dt_bias", vp),
         ("out", vp), ("out_bs", i64),
+        ("state_batch_indices", vp), ("state_batch", i64),
     ]
 
 

@@ -14,9 +14,10 @@ from .selective_scan_cuda import _itype, _ptr, _stream, _req
 
 def selective_state_update(state, x, dt, A, B, C, D=None, z=None, dt_bias=None, dt_softplus=False,
                            state_batch_indices=None):
-    if state_batch_indices is not None:
-        raise NotImplementedError("selective_state_update: state_batch_indices is not supported")
-    a, out = _state_args(state, x, dt, A, B, C, D, z, dt_bias, dt_softplus)
+    """state_batch_indices (batch,): batch row b reads and updates state row
+    state_batch_indices[b] (continuous batching); a negative index marks a padding row,
+    whose state is untouched and whose output is zero."""
+    a, out = _state_args(state, x, dt, A, B, C, D, z, dt_bias, dt_softplus, state_batch_indices)
     with torch.cuda.device(x.device):
         check(lib.ssm_state_update(ctypes.byref(a), _stream(x.device)))
     return out
@@ -47,10 +48,17 @@ def selective_state_update_dtproj(state, x, dt_in, dt_proj_weight, A, B, C, D=No
     return out
 
 
-def _state_args(state, x, dt, A, B, C, D, z, dt_bias, dt_softplus):
+def _state_args(state, x, dt, A, B, C, D, z, dt_bias, dt_softplus, state_batch_indices=None):
     if state.dim() != 3:
         raise NotImplementedError("selective_state_update: only the (batch, dim, dstate) layout is supported")
-    batch, dim, dstate = state.shape
+    state_batch, dim, dstate = state.shape
+    batch = x.shape[0]
+    if state_batch_indices is None:
+        _req(state_batch == batch, "state and x must have the same batch size")
+    else:
+        _req(state_batch_indices.shape == (batch,) and state_batch_indices.is_cuda,
+             "state_batch_indices must be a (batch,) CUDA tensor")
+        state_batch_indices = state_batch_indices.to(torch.int32).contiguous()
     _req(x.shape == (batch, dim) and (dt is None or dt.shape == (batch, dim)), "x and dt must be (batch, dim)")
     _req(dt is None or x.dtype == dt.dtype, "x and dt must share a dtype")
     _req(A.shape == (dim, dstate) and A.dtype == torch.float32, "A must be float32 (dim, dstate)")
@@ -97,4 +105,7 @@ def _state_args(state, x, dt, A, B, C, D, z, dt_bias, dt_softplus):
         a.z, a.z_bs = _ptr(z), z.stride(0)
     a.dt_bias = _ptr(dt_bias)
     a.out, a.out_bs = _ptr(out), out.stride(0)
+    if state_batch_indices is not None:
+        a.state_batch_indices, a.state_batch = _ptr(state_batch_indices), state_batch
+        a._keep = state_batch_indices  # alive until the launch is queued
     return a, out

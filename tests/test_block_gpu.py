@@ -97,6 +97,37 @@ def test_state_update_decode_config2_shape(dtype, state_dtype):
     assert_close(st, ref_state, t, t, "state")
 
 
+@pytest.mark.parametrize("n,state_dtype", [(16, torch.float32), (16, torch.bfloat16), (24, torch.float32)])
+def test_state_update_with_state_batch_indices(n, state_dtype):
+    """Continuous batching: batch row b updates state row idx[b]; -1 (padding) and an index past
+    the state's rows leave the state alone and give a zero output row."""
+    from motif_ssm import selective_state_update
+    batch, dim, slots = 6, 64, 9
+    g = torch.Generator().manual_seed(3)
+    state = torch.randn(slots, dim, n, generator=g).to(state_dtype)
+    x, dt, z = (torch.randn(batch, dim, generator=g) for _ in range(3))
+    A = -torch.arange(1, n + 1, dtype=torch.float32).repeat(dim, 1)
+    B, C = torch.randn(batch, n, generator=g), torch.randn(batch, n, generator=g)
+    D, dt_bias = torch.randn(dim, generator=g), torch.randn(dim, generator=g)
+    idx = torch.tensor([7, 0, -1, 3, 9, 5], dtype=torch.int64)
+    ref_state = state.clone()
+    ref = torch.zeros(batch, dim)
+    for b, sb in enumerate(idx.tolist()):
+        if 0 <= sb < slots:
+            row = ref_state[sb:sb + 1]
+            ref[b] = O.selective_state_update_ref(row, x[b:b + 1], dt[b:b + 1], A, B[b:b + 1], C[b:b + 1], D,
+                                                  z=z[b:b + 1], dt_bias=dt_bias, dt_softplus=True)[0]
+            ref_state[sb] = row[0]
+    st = state.to(DEV)
+    out = selective_state_update(st, x.to(DEV), dt.to(DEV), A.to(DEV), B.to(DEV), C.to(DEV), D.to(DEV),
+                                 z=z.to(DEV), dt_bias=dt_bias.to(DEV), dt_softplus=True,
+                                 state_batch_indices=idx.to(DEV))
+    t = 1e-5 if state_dtype == torch.float32 else tol(torch.bfloat16)
+    assert_close(out, ref, t, t, "y")
+    assert_close(st, ref_state, t, t, "state")
+    assert out[2].abs().max().item() == 0 and out[4].abs().max().item() == 0
+
+
 def test_mamba_inner_matches_reference_golden():
     from motif_ssm import mamba_inner_fn
     rec = torch.load(os.path.join(GOLD, "inner_small.pt"), weights_only=False)
