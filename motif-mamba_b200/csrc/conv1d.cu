@@ -11,8 +11,9 @@
 //
 // Both directions are HBM-streaming: one warp walks one (b, c) row in steps of 256
 // timesteps, each lane owning 8 consecutive outputs read with 16-byte vector loads.  The
-// W-1 halo comes from the neighbouring vector (an L1 hit).  Weight gradients are kept
-// per lane, reduced across the warp with shuffles and added once per row.
+// forward reads its W-1 halo from the neighbouring vector (an L1 hit); the backward takes
+// both halos from neighbouring lanes by shuffle.  Weight gradients are kept per lane,
+// reduced across the warp with shuffles and added once per row.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -78,13 +79,21 @@ __global__ void __launch_bounds__(256) conv1d_fwd_kernel(const conv1d_args a, in
     }
 }
 
+// Backward: each lane computes dpre only at its own 8 positions.  The W-1 values of x before
+// its block come from the lane below by shuffle (lane 0: lane 31 of the previous 256-step
+// step, kept in registers), and the W-1 values of dpre after its block from the lane above;
+// lane 31's next values belong to lane 0 of the NEXT step, so lane 31 writes its dx one step
+// late.  Per 8 outputs: two 16-byte loads (x, dout) and 8 sigmoids.
 template <typename T, typename WT, int KW>
 __global__ void __launch_bounds__(256) conv1d_bwd_kernel(const conv1d_args a, int vec) {
+    constexpr int H = KW - 1;  // halo
+    constexpr unsigned FULL = 0xffffffffu;
     const int lane = threadIdx.x & 31;
     const int64_t nrows = a.batch * a.dim;
     const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
     const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-    for (int64_t r = warp; r < nrows; r += nwarps) {
+    const int64_t L = a.seqlen;
+    for (int64_t r = warp; r < nrows; r += nwarps) {  // uniform per warp
         const int64_t b = r / a.dim, c = r - b * a.dim;
         float w[KW];
 #pragma unroll
@@ -96,55 +105,90 @@ __global__ void __launch_bounds__(256) conv1d_bwd_kernel(const conv1d_args a, in
         float dw[KW], db = 0.f;
 #pragma unroll
         for (int k = 0; k < KW; ++k) dw[k] = 0.f;
-        for (int64_t t0 = (int64_t)lane * 8; t0 < a.seqlen; t0 += 256) {
-            // x over [t0-8, t0+16), dout over [t0, t0+16)
-            float xp[8], xc[8], xn[8], dc[8], dn[8];
-            load8_row(xr, t0 - 8, a.seqlen, vec, xp);
-            load8_row(xr, t0, a.seqlen, vec, xc);
-            load8_row(xr, t0 + 8, a.seqlen, vec, xn);
-            load8_row(dor, t0, a.seqlen, vec, dc);
-            load8_row(dor, t0 + 8, a.seqlen, vec, dn);
-            auto xat = [&](int j) -> float {  // x at t0 + j, j in [-8, 16)
-                return j < 0 ? xp[8 + j] : (j < 8 ? xc[j] : xn[j - 8]);
-            };
-            // dpre at t0 + i for i in [0, 8 + KW - 1)
-            float dpre[8 + KW - 1];
+        float xcarry[H + 1], dprev[8];  // lane 31's last x of the previous step; lane 31's pending dpre
 #pragma unroll
-            for (int i = 0; i < 8 + KW - 1; ++i) {
+        for (int h = 0; h <= H; ++h) xcarry[h] = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dprev[i] = 0.f;
+        int64_t tb = 0;
+        for (; tb < L; tb += 256) {  // uniform: lanes past L see zeros
+            const int64_t t0 = tb + (int64_t)lane * 8;
+            float xc[8], dc[8];
+            load8_row(xr, t0, L, vec, xc);
+            load8_row(dor, t0, L, vec, dc);
+            float xh[H + 1];  // x at t0 - H .. t0 - 1 (index H unused)
+#pragma unroll
+            for (int h = 0; h < H; ++h) {
+                const float up = __shfl_up_sync(FULL, xc[8 - H + h], 1);
+                xh[h] = lane == 0 ? xcarry[h] : up;
+                xcarry[h] = __shfl_sync(FULL, xc[8 - H + h], 31);
+            }
+            auto xat = [&](int j) -> float { return j < 0 ? xh[H + j] : xc[j]; };  // x at t0 + j
+            float dpre[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
                 float pre = bias;
 #pragma unroll
-                for (int k = 0; k < KW; ++k) pre = fmaf(w[k], xat(i - (KW - 1) + k), pre);
-                const float dov = i < 8 ? dc[i] : dn[i - 8];  // zero beyond L (load8_row fills 0)
-                float g = dov;
+                for (int k = 0; k < KW; ++k) pre = fmaf(w[k], xat(i - H + k), pre);
+                float g = dc[i];  // zero beyond L
                 if (a.silu) {
                     const float s = sigmoidf_(pre);
-                    g = dov * s * (1.f + pre * (1.f - s));
+                    g = g * s * (1.f + pre * (1.f - s));
                 }
                 dpre[i] = g;
+                db += g;
+#pragma unroll
+                for (int k = 0; k < KW; ++k) dw[k] = fmaf(g, xat(i - H + k), dw[k]);
             }
+            // dx[t] = sum_k w[k] dpre[t + H - k]: lanes 0-30 finish this step's block, lane 31
+            // the previous step's, with the first H dpre of lane 0 of this step
+            float nxt[H + 1];
+#pragma unroll
+            for (int h = 0; h < H; ++h) {
+                const float dn = __shfl_down_sync(FULL, dpre[h], 1);
+                const float d0 = __shfl_sync(FULL, dpre[h], 0);
+                nxt[h] = lane == 31 ? d0 : dn;
+            }
+            float src[8], dxv[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) src[i] = lane == 31 ? dprev[i] : dpre[i];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                float acc = 0.f;
+#pragma unroll
+                for (int k = 0; k < KW; ++k) {
+                    const int j = i + H - k;
+                    acc = fmaf(w[k], j < 8 ? src[j] : nxt[j - 8], acc);
+                }
+                dxv[i] = acc;
+            }
+            const int64_t ts = lane == 31 ? t0 - 256 : t0;
+            if (ts >= 0 && ts < L) store8_row(dxr, ts, L, vec, dxv);
+            if (lane == 31) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) dprev[i] = dpre[i];
+            }
+        }
+        if (lane == 31) {  // the last step's block: nothing follows it (dpre beyond L is zero)
+            const int64_t ts = tb - 256 + 248;
             float dxv[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
                 float acc = 0.f;
 #pragma unroll
-                for (int k = 0; k < KW; ++k) acc = fmaf(w[k], dpre[i + (KW - 1) - k], acc);
+                for (int k = 0; k < KW; ++k) {
+                    const int j = i + H - k;
+                    acc = fmaf(w[k], j < 8 ? dprev[j] : 0.f, acc);
+                }
                 dxv[i] = acc;
             }
-            store8_row(dxr, t0, a.seqlen, vec, dxv);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                if (t0 + i < a.seqlen) {
-                    db += dpre[i];
-#pragma unroll
-                    for (int k = 0; k < KW; ++k) dw[k] = fmaf(dpre[i], xat(i - (KW - 1) + k), dw[k]);
-                }
-            }
+            if (ts >= 0 && ts < L) store8_row(dxr, ts, L, vec, dxv);
         }
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) {
-            db += __shfl_xor_sync(0xffffffffu, db, off);
+            db += __shfl_xor_sync(FULL, db, off);
 #pragma unroll
-            for (int k = 0; k < KW; ++k) dw[k] += __shfl_xor_sync(0xffffffffu, dw[k], off);
+            for (int k = 0; k < KW; ++k) dw[k] += __shfl_xor_sync(FULL, dw[k], off);
         }
         if (lane == 0) {
 #pragma unroll

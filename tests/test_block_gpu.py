@@ -20,6 +20,12 @@ DEV = "cuda"
     (1, 33, 1, 4, torch.float32, torch.float32, False, True),
     (3, 16, 77, 3, torch.float16, torch.float32, True, False),
     (2, 8, 40, 2, torch.bfloat16, torch.float32, True, True),
+    # 256-step boundaries (lane 31's block finishes a step late) and ragged tails
+    (1, 8, 256, 4, torch.float32, torch.float32, True, True),
+    (2, 8, 512, 4, torch.bfloat16, torch.bfloat16, True, True),
+    (1, 5, 1031, 3, torch.float32, torch.float32, False, True),
+    (1, 4, 2049, 2, torch.float32, torch.float32, True, False),
+    (2, 6, 264, 4, torch.float16, torch.float16, True, True),
 ])
 def test_causal_conv1d_fwd_bwd(batch, dim, seqlen, width, dtype, wdtype, bias, silu):
     from motif_ssm import causal_conv1d_fn
