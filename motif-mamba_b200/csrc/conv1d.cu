@@ -83,9 +83,10 @@ __global__ void __launch_bounds__(256) conv1d_fwd_kernel(const conv1d_args a, in
 // its block come from the lane below by shuffle (lane 0: lane 31 of the previous 256-step
 // step, kept in registers), and the W-1 values of dpre after its block from the lane above;
 // lane 31's next values belong to lane 0 of the NEXT step, so lane 31 writes its dx one step
-// late.  Per 8 outputs: two 16-byte loads (x, dout) and 8 sigmoids.
+// late.  Per 8 outputs: two 16-byte loads (x, dout) and 8 sigmoids.  The kernel is bound by
+// load latency, so it is held to 64 registers for 4 resident CTAs per SM (3 at 80: 11 % slower).
 template <typename T, typename WT, int KW>
-__global__ void __launch_bounds__(256) conv1d_bwd_kernel(const conv1d_args a, int vec) {
+__global__ void __launch_bounds__(256, 4) conv1d_bwd_kernel(const conv1d_args a, int vec) {
     constexpr int H = KW - 1;  // halo
     constexpr unsigned FULL = 0xffffffffu;
     const int lane = threadIdx.x & 31;
