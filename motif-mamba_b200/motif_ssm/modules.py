@@ -148,18 +148,28 @@ class Mambamotif(nn.Module):
             p.requires_grad_(True)
 
     def _decode_consts(self):
-        """A = -exp(A_log) and the fp32 dt bias for decode steps, recomputed only when
-        A_log or the bias change (tracked by their version counters and storage), so a
-        decode step does not launch two elementwise kernels and a cast per layer for them.
-        A CUDA graph captured over ``step`` reads these cached tensors: in-place edits of
-        A_log / dt_proj.bias after capture need a new capture."""
+        """A = -exp(A_log), the fp32 dt bias and the fp32 D for inference, recomputed only
+        when A_log, the bias or D change (tracked by their version counters and storage), so
+        a prefill or decode step does not launch the elementwise kernels and casts per layer
+        for them.  A CUDA graph captured over ``forward`` / ``step`` reads these cached
+        tensors: in-place edits of A_log / dt_proj.bias / D after capture need a new capture."""
         key = (self.A_log._version, self.A_log.data_ptr(), self.dt_proj.bias._version,
-               self.dt_proj.bias.data_ptr())
+               self.dt_proj.bias.data_ptr(), self.D._version, self.D.data_ptr())
         if getattr(self, "_dc_key", None) != key:
             with torch.no_grad():
-                self._dc = (-torch.exp(self.A_log.float()), self.dt_proj.bias.float().contiguous())
+                self._dc = (-torch.exp(self.A_log.float()), self.dt_proj.bias.float().contiguous(),
+                            self.D.float().contiguous())
             self._dc_key = key
         return self._dc
+
+    def _scan_consts(self):
+        """(A, D, dt bias) in fp32 for the scan: cached when no gradient can flow to them,
+        otherwise computed in the autograd graph."""
+        if torch.is_grad_enabled() and (self.A_log.requires_grad or self.D.requires_grad
+                                        or self.dt_proj.bias.requires_grad):
+            return -torch.exp(self.A_log.float()), self.D.float(), self.dt_proj.bias.float()
+        A, dt_bias, D = self._decode_consts()
+        return A, D, dt_bias
 
     def _P_eff(self):
         return None if self.P is None else self.pq_k * self.P
@@ -178,11 +188,11 @@ class Mambamotif(nn.Module):
         xz = xz.transpose(0, 1)
         if self.in_proj.bias is not None:
             xz = xz + self.in_proj.bias.to(xz.dtype).unsqueeze(-1)
-        A = -torch.exp(self.A_log.float())
+        A, D, dt_bias = self._scan_consts()
         if self.use_fast_path and self.P is None and inference_params is None:
             return mamba_inner_fn(xz, self.conv1d.weight, self.conv1d.bias, self.x_proj.weight,
                                   self.dt_proj.weight, self.out_proj.weight, self.out_proj.bias, A, None, None,
-                                  self.D.float(), delta_bias=self.dt_proj.bias.float(), delta_softplus=True)
+                                  D, delta_bias=dt_bias, delta_softplus=True)
         x, z = xz.chunk(2, dim=1)
         if conv_state is not None:
             conv_state.copy_(F.pad(x, (self.d_conv - x.shape[-1], 0)))
@@ -193,7 +203,7 @@ class Mambamotif(nn.Module):
         dt = (self.dt_proj.weight @ dt.t()).view(self.d_inner, batch, seqlen).transpose(0, 1)
         B = B.view(batch, seqlen, -1).transpose(1, 2).contiguous()
         C = C.view(batch, seqlen, -1).transpose(1, 2).contiguous()
-        y = selective_scan_fn(x, dt, A, B, C, self.D.float(), z=z, delta_bias=self.dt_proj.bias.float(),
+        y = selective_scan_fn(x, dt, A, B, C, D, z=z, delta_bias=dt_bias,
                               delta_softplus=True, return_last_state=ssm_state is not None,
                               P=self._P_eff(), Q=self.Q)
         if ssm_state is not None:
@@ -217,7 +227,7 @@ class Mambamotif(nn.Module):
         dt, B, C = torch.split(x_db, [self.dt_rank, self.d_state, self.d_state], dim=-1)
         if self.P is None and dtproj_supported(ssm_state, x, dt, self.dt_proj.weight):
             # dt_proj folded into the state update kernel (same rounding of dt as the GEMM)
-            A, dt_bias = self._decode_consts()
+            A, dt_bias, _ = self._decode_consts()
             y = selective_state_update_dtproj(ssm_state, x, dt, self.dt_proj.weight, A, B, C, self.D, z=z,
                                               dt_bias=dt_bias, dt_softplus=True)
             return self.out_proj(y).unsqueeze(1), conv_state, ssm_state
@@ -231,7 +241,7 @@ class Mambamotif(nn.Module):
                                               P=self._P_eff(), Q=self.Q)
             ssm_state.copy_(last_state.to(ssm_state.dtype))
             return self.out_proj(y[..., 0]).unsqueeze(1), conv_state, ssm_state
-        A, dt_bias = self._decode_consts()
+        A, dt_bias, _ = self._decode_consts()
         y = selective_state_update(ssm_state, x, dt, A, B, C, self.D, z=z, dt_bias=dt_bias, dt_softplus=True)
         return self.out_proj(y).unsqueeze(1), conv_state, ssm_state
 
@@ -469,7 +479,10 @@ class TPMambamotif(nn.Module):
         dt = (self.dt_proj_w @ dt.t()).view(self.d_local, batch, seqlen).transpose(0, 1)
         B = B.reshape(batch, seqlen, -1).transpose(1, 2).contiguous()
         C = C.reshape(batch, seqlen, -1).transpose(1, 2).contiguous()
-        y = selective_scan_fn(x, dt, -torch.exp(self.A_log), B, C, self.D, z=z, delta_bias=self.dt_proj_b,
+        key = (self.A_log._version, self.A_log.data_ptr())
+        if getattr(self, "_A_key", None) != key:  # A = -exp(A_log), once per change of A_log
+            self._A, self._A_key = -torch.exp(self.A_log), key
+        y = selective_scan_fn(x, dt, self._A, B, C, self.D, z=z, delta_bias=self.dt_proj_b,
                               delta_softplus=True, P=self.P_eff, Q=self.Q)
         out = y.transpose(1, 2).reshape(-1, self.d_local) @ self.out_proj_w.t()
         return self._all_reduce(out.contiguous()).view(batch, seqlen, self.d_model)  # all-reduce #2
