@@ -209,6 +209,23 @@ __global__ void conv1d_update_kernel(const conv1d_update_args a) {
     const int S = (int)a.state_len, KW = (int)a.width;
     float acc = a.bias ? ldw<WT>(a.bias, c) : 0.f;
     // shift left by one and append x; the taps read the newest KW entries
+    if (S <= 8) {  // the window in registers: all loads issue before the first store
+        float v[8];
+#pragma unroll
+        for (int s = 0; s < 8; ++s) v[s] = s < S ? to_f<ST>(st[s]) : 0.f;
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+            if (s < S) {
+                const ST nv = from_f<ST>(s + 1 < 8 && s + 1 < S ? v[s + 1] : xv);
+                st[s] = nv;
+                const int k = s - (S - KW);
+                if (k >= 0) acc = fmaf(ldw<WT>(a.weight, c * a.w_ds + k * a.w_ks), to_f<ST>(nv), acc);
+            }
+        }
+        if (a.silu) acc = acc * sigmoidf_(acc);
+        reinterpret_cast<T *>(a.out)[b * a.out_bs + c] = from_f<T>(acc);
+        return;
+    }
     for (int s = 0; s < S; ++s) {
         const float v = s + 1 < S ? to_f<ST>(st[s + 1]) : xv;
         st[s] = from_f<ST>(v);

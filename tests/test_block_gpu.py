@@ -49,6 +49,29 @@ def test_causal_conv1d_fwd_bwd(batch, dim, seqlen, width, dtype, wdtype, bias, s
         assert_close(dl[2].grad, leaves[2].grad, t, t, "conv dbias")
 
 
+@pytest.mark.parametrize("state_len,width,dtype,sdtype", [
+    (4, 4, torch.bfloat16, torch.bfloat16), (6, 4, torch.float32, torch.float32),
+    (3, 3, torch.float16, torch.float32), (10, 4, torch.bfloat16, torch.float32)])
+def test_conv_update_state_lengths(state_len, width, dtype, sdtype):
+    """Decode conv step for state windows longer than the taps (the newest `width` entries
+    are used) in registers (<= 8) and in the loop path (> 8); two steps in a row."""
+    from motif_ssm import causal_conv1d_update
+    g = torch.Generator().manual_seed(state_len)
+    batch, dim = 5, 40
+    st = torch.randn(batch, dim, state_len, generator=g).to(sdtype)
+    w = (0.5 * torch.randn(dim, width, generator=g)).to(dtype)
+    bias = (0.1 * torch.randn(dim, generator=g)).to(dtype)
+    st_dev = st.to(DEV)
+    for step in range(2):
+        x = torch.randn(batch, dim, generator=g).to(dtype)
+        st = torch.cat([st[..., 1:], x.to(sdtype).unsqueeze(-1)], dim=-1)
+        y = torch.nn.functional.silu((st[..., -width:].float() * w.float()).sum(-1) + bias.float()).to(dtype)
+        out = causal_conv1d_update(x.to(DEV), st_dev, w.to(DEV), bias.to(DEV), "silu")
+        t = tol(dtype)
+        assert_close(out, y, t, t, f"conv update out, step {step}")
+        assert_close(st_dev, st, 1e-6, 1e-6, f"conv state, step {step}")
+
+
 def test_conv_update_and_state_update_match_module_golden():
     """Replays Mambamotif.step's decode steps (golden from the reference's own module)
     with causal_conv1d_update + selective_state_update on the GPU."""
