@@ -160,9 +160,21 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(rows), "samples_under_load": len(loaded)}
 
 
+CPU_SAMPLE_DIM = 64  # channels of the fixed CPU sample: batch 1 x 64 x seqlen, seed 0
+
+
+def cpu_threads():
+    """Host threads this process may run on (its CPU affinity, not the machine's core count:
+    oversubscribing the affinity set slows the oracle's per-step loop several-fold)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
 def _cpu_scan_seconds(dim_s):
     """Seconds for the oracle restatement of selective_scan_ref (fwd + autograd bwd) on
-    batch 1 x dim_s channels x seqlen 4096 (bf16 inputs, fp32 math)."""
+    batch 1 x dim_s channels x the workload's seqlen (bf16 inputs, fp32 math), seed 0."""
     from oracle import ssm_oracle as O
     l, n = CFG["seqlen"], CFG["dstate"]
     g = torch.Generator().manual_seed(0)
@@ -178,51 +190,52 @@ def _cpu_scan_seconds(dim_s):
     return time.perf_counter() - t0
 
 
-def _cpu_sample_dim(budget_s):
-    """Channels of a CPU sample that takes about `budget_s`: a warmed-up probe, then one
-    refinement (the oracle's time is not linear in the channel count: per-step overheads at
-    small counts, cache spills at large ones)."""
-    probe = 8
-    _cpu_scan_seconds(probe)  # warm-up
-    tp = _cpu_scan_seconds(probe)
-    dim_s = int(max(probe, min(CFG["dim"], probe * budget_s / max(tp, 1e-3))))
-    t1 = _cpu_scan_seconds(dim_s)
-    return int(max(probe, min(CFG["dim"], dim_s * budget_s / max(t1, 1e-3))))
-
-
-def _cpu_record(dim_s, dt):
+def _cpu_record(dim_s, dt, threads, n_samples):
     l, n = CFG["seqlen"], CFG["dstate"]
     f, b = algo_bytes(1, dim_s, l, n)
-    return dict(value=(f + b) / dt / 1e9, unit="GB/s", cores=torch.get_num_threads(), kind="port",
-                sample=f"selective_scan_ref fwd + autograd bwd (oracle restatement), batch 1 x {dim_s} channels "
-                       f"x seqlen {l}, n {n}, bf16 inputs, fp32 math: {dt:.2f} s per sample "
-                       f"({dim_s * l / dt / 1e6:.3f} M elements/s); metric scaled by the algorithmic bytes of the sample")
+    return dict(value=(f + b) / dt / 1e9, unit="GB/s", cores=threads, kind="port",
+                m_elements_per_s=dim_s * l / dt / 1e6,
+                sample=f"selective_scan_ref fwd + autograd bwd (oracle restatement), fixed sample batch 1 x {dim_s} "
+                       f"channels x seqlen {l}, n {n}, seed 0, bf16 inputs, fp32 math, {threads} threads: median "
+                       f"{dt:.2f} s over {n_samples} timed samples after 1 warm-up ({dim_s * l / dt / 1e6:.4f} M "
+                       f"elements/s); GB/s = the sample's algorithmic bytes (the metric's formula at batch 1 x "
+                       f"{dim_s} channels) / its time, i.e. the same per-element rate applied to the full workload")
 
 
-def cpu_baseline_sample(threads=None, budget_s=15.0):
-    if threads:
-        torch.set_num_threads(threads)
-    dim_s = _cpu_sample_dim(budget_s)
-    dt = _cpu_scan_seconds(dim_s)
-    return _cpu_record(dim_s, dt), dt
+def cpu_baseline_sample(n_timed=2):
+    """The repo arm's cpu_baseline: the same fixed sample and thread count as the reference arm."""
+    threads = cpu_threads()
+    torch.set_num_threads(threads)
+    _cpu_scan_seconds(CPU_SAMPLE_DIM)  # warm-up (first-call costs)
+    ts = [_cpu_scan_seconds(CPU_SAMPLE_DIM) for _ in range(n_timed)]
+    dt = statistics.median(ts)
+    return _cpu_record(CPU_SAMPLE_DIM, dt, threads, n_timed), dt
 
 
-def run_reference(args):
+def run_reference(args, budget_s=200.0):
+    """The reference arm: the oracle port of the reference's CPU path on all host threads of this
+    process, one fixed sample per step.  One warm-up sample, then up to --steps timed samples;
+    sampling stops early once ~budget_s seconds have been spent so the run stays within a few
+    minutes at any --steps (the line says how many samples were timed)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    torch.set_num_threads(os.cpu_count() or 1)
-    dim_s = _cpu_sample_dim(max(1.0, 120.0 / (args.warmup + args.steps)))
+    threads = cpu_threads()
+    torch.set_num_threads(threads)
+    t_start = time.perf_counter()
+    _cpu_scan_seconds(CPU_SAMPLE_DIM)
     times = []
-    for i in range(args.warmup + args.steps):
-        dt = _cpu_scan_seconds(dim_s)
-        if i >= args.warmup:
-            times.append(dt)
-    cb = _cpu_record(dim_s, statistics.median(times))
+    for i in range(args.steps):
+        times.append(_cpu_scan_seconds(CPU_SAMPLE_DIM))
+        if time.perf_counter() - t_start > budget_s:
+            break
+    dt = statistics.median(times)
+    cb = _cpu_record(CPU_SAMPLE_DIM, dt, threads, len(times))
     v = cb["value"]
     fwd_b, bwd_b = algo_bytes(**CFG)
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": (fwd_b + bwd_b) / (v * 1e9) * 1e3,
+            "steps": args.steps, "warmup": args.warmup, "samples_timed": len(times),
+            "ms_per_step": (fwd_b + bwd_b) / (v * 1e9) * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic", "config": {"workload": "selective scan fwd+bwd, BASELINE config 4 at seqlen 4096 "
                                                         "(32 x 3072 x 4096, n 16, bf16 I/O)",
@@ -245,11 +258,15 @@ def main():
     ap.add_argument("--batch", type=int, default=None,
                     help="override the per-GPU batch (profiling a smaller case of the same kernels)")
     ap.add_argument("--seqlen", type=int, default=None, help="override the sequence length")
-    ap.add_argument("--workload", default="scan", choices=["scan", "prefill", "tp", "pq"],
+    ap.add_argument("--once", action="store_true", help="kernels workload: run each kernel twice (ncu capture)")
+    ap.add_argument("--quick", action="store_true", help="refkernel workload: config 4 at seqlen 1024 only")
+    ap.add_argument("--workload", default="scan", choices=["scan", "prefill", "tp", "pq", "kernels", "refkernel"],
                     help="scan: selective scan fwd+bwd, config 4 (default); prefill: 24-layer config-2 stack, "
                          "prefill tok/s (global batch 16 x 4096, strong scaling) plus greedy decode tok/s; "
                          "tp: 64-layer config-3 stack, prefill 1 x 32768 with d_inner sharded over the GPUs; "
-                         "pq: the motif P/Q-coupled scan fwd+bwd at a config-1 block's shape")
+                         "pq: the motif P/Q-coupled scan fwd+bwd at a config-1 block's shape; "
+                         "kernels: conv1d / add+RMSNorm / decode kernels' GB/s; "
+                         "refkernel: our scan kernels timed beside the reference's CUDA extension")
     args = ap.parse_args()
     if args.batch:
         CFG["batch"] = args.batch
@@ -262,6 +279,10 @@ def main():
         return run_tp(args)
     if args.workload == "pq":
         return run_pq(args)
+    if args.workload == "kernels":
+        return run_kernels(args)
+    if args.workload == "refkernel":
+        return run_refkernel(args)
     if args.impl == "reference":
         return run_reference(args)
 
@@ -331,7 +352,7 @@ def main():
     traffic = ncu_traffic(dom_name)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu, _ = cpu_baseline_sample(os.cpu_count(), budget_s=15.0)
+        cpu, _ = cpu_baseline_sample()
     if rank == 0:
         clocks = clk.summary()
         line = {
@@ -512,7 +533,7 @@ def run_prefill(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         if rank == 0:
-            cb = _cpu_prefill_tok_s(os.cpu_count() or 1)
+            cb = _cpu_prefill_tok_s(cpu_threads())
             print(json.dumps({"impl": "reference", "metric": "MotifMamba prefill tok/s (config 2)", "value": cb["value"],
                               "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                               "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
@@ -599,7 +620,7 @@ def run_prefill(args):
     te = torch.tensor([s.elapsed_time(e) / args.steps], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    cpu = _cpu_prefill_tok_s(os.cpu_count() or 1) if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
+    cpu = _cpu_prefill_tok_s(cpu_threads()) if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
     if rank == 0:
         print(json.dumps({
             "metric": "MotifMamba prefill tok/s (config 2)", "value": value, "unit": "tok/s", "n_gpus": world,
@@ -678,7 +699,7 @@ def run_pq(args):
            "l2": "working set per step ~0.45 GB (9 tensors of 50 MB) > 126 MB L2, no flush"}
     if args.impl == "reference":
         if rank == 0:
-            cb = _cpu_pq_record(os.cpu_count() or 1, 20.0)
+            cb = _cpu_pq_record(cpu_threads(), 20.0)
             print(json.dumps({"impl": "reference", "metric": metric, "value": cb["value"], "unit": cb["unit"],
                               "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
                               "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
@@ -729,7 +750,7 @@ def run_pq(args):
     fwd_ms = statistics.median(a.elapsed_time(bq) for a, bq, _ in evs)
     bwd_ms = statistics.median(bq.elapsed_time(c) for _, bq, c in evs)
     el = b * d * l * n
-    cpu = _cpu_pq_record(os.cpu_count() or 1, 15.0) if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
+    cpu = _cpu_pq_record(cpu_threads(), 15.0) if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
     if rank == 0:
         print(json.dumps({"metric": metric, "value": el * world / (ms * 1e-3) / 1e9, "unit": "G element-states/s",
                           "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
@@ -800,6 +821,179 @@ def run_tp(args):
             "clocks": clk.summary(), "e2e": None, "cpu_baseline": None}), flush=True)
     if world > 1:
         dist.destroy_process_group()
+    return 0
+
+
+def _median_ms(fn, warmup=3, iters=10, reps=10):
+    """Median over ``iters`` of the mean time of ``reps`` back-to-back calls (the host's
+    launch overhead overlaps the queued kernels instead of adding idle gaps)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(iters):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(reps):
+            fn()
+        e.record()
+        e.synchronize()
+        ts.append(s.elapsed_time(e) / reps)
+    return statistics.median(ts)
+
+
+def _nbytes(*ts):
+    return sum(t.numel() * t.element_size() for t in ts if t is not None)
+
+
+def run_kernels(args):
+    """Achieved HBM bandwidth of the kernels around the scan: causal conv1d forward / backward,
+    the fused residual add + RMSNorm, and the two decode kernels (conv1d update and the SSM state
+    update); one JSON line per kernel (CUDA-event medians).  ``--once`` runs each kernel twice
+    instead, for an ncu launch capture.
+
+    Shapes: the conv and the norm at BASELINE config 2's prefill (16 x 4096 tokens, d_inner 1536,
+    d_model 768, bf16; every tensor > 126 MB L2 except the conv weights), the decode kernels at
+    its decode step (batch 64, d_inner 1536, d_state 16), whose few MB stay in L2: those two are
+    launch- and latency-bound and their GB/s says so.  Bytes are the algorithmic ones: every
+    input read once, every output written once."""
+    if args.impl == "reference":
+        print(json.dumps({"impl": "reference", "unavailable": "the kernels workload has no CPU reference run; "
+                          "use the default scan workload for the reference arm"}))
+        return 0
+    from motif_ssm import causal_conv1d as cc
+    from motif_ssm.norm import add_rms_norm
+    from motif_ssm.selective_state_update import selective_state_update
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    r = lambda *s, dt=torch.bfloat16: torch.randn(*s, device=dev, generator=g).to(dt)
+    b, d, l, dm = 16, 1536, 4096, 768
+    x, dout = r(b, d, l), r(b, d, l)
+    w, bias = r(d, 4), r(d)
+    xs, res, nw = r(b * l, dm), r(b * l, dm, dt=torch.float32), r(dm)
+    db, n = 64, 16
+    state, conv_state = r(db, d, n), r(db, d, 4)
+    xd, dtd, zd = r(db, d), r(db, d), r(db, d)
+    A = -torch.arange(1, n + 1, device=dev, dtype=torch.float32).repeat(d, 1)
+    Bd, Cd = r(db, n), r(db, n)
+    D, dt_bias = r(d, dt=torch.float32), r(d, dt=torch.float32)
+    work = [
+        ("conv1d_fwd", "16 x 1536 x 4096 bf16, SiLU",
+         lambda: cc.causal_conv1d_fwd_function(x, w, bias, None, None, None, True),
+         2 * _nbytes(x) + _nbytes(w, bias)),
+        ("conv1d_bwd", "16 x 1536 x 4096 bf16, SiLU",
+         lambda: cc.causal_conv1d_bwd_function(x, w, bias, dout, None, None, None, None, False, True),
+         3 * _nbytes(x) + _nbytes(w, bias) + 4 * (w.numel() + bias.numel())),
+        ("add_rms_norm", "65536 x 768, bf16 x / out, fp32 residual in / out",
+         lambda: add_rms_norm(xs, res, nw, 1e-5, True),
+         2 * _nbytes(xs) + 2 * _nbytes(res) + _nbytes(nw)),
+        ("conv1d_update", "decode, 64 x 1536, width 4, bf16",
+         lambda: cc.causal_conv1d_update_function(xd, conv_state, w, bias, True, None, None),
+         2 * _nbytes(xd) + 2 * _nbytes(conv_state) + _nbytes(w, bias)),
+        ("ssm_state_update", "decode, 64 x 1536 x 16, bf16 state, z, D, dt_bias",
+         lambda: selective_state_update(state, xd, dtd, A, Bd, Cd, D, z=zd, dt_bias=dt_bias, dt_softplus=True),
+         2 * _nbytes(state) + 4 * _nbytes(xd) + _nbytes(A, Bd, Cd, D, dt_bias)),
+    ]
+    peak, _ = hbm_peak()
+    for name, shape, fn, nbytes in work:
+        if args.once:
+            fn()
+            fn()
+            torch.cuda.synchronize()
+            continue
+        ms = _median_ms(fn)
+        print(json.dumps({"kernel": name, "shape": shape, "ms": round(ms, 5), "bytes": nbytes,
+                          "GB/s": round(nbytes / (ms * 1e-3) / 1e9, 1),
+                          "frac_of_hbm": round(nbytes / (ms * 1e-3) / 1e9 / peak, 3)}), flush=True)
+    return 0
+
+
+def _time_median(fn, warmup, iters):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(iters):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        e.synchronize()
+        ts.append(s.elapsed_time(e))
+    return statistics.median(ts)
+
+
+def _refk_inputs(b, d, l, n, dtype, z=True, pq_rank=0, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    r = lambda *s: torch.randn(*s, device="cuda", generator=g)
+    t = dict(u=r(b, d, l).to(dtype), delta=r(b, d, l).to(dtype), z=r(b, d, l).to(dtype) if z else None,
+             B=r(b, 1, n, l).to(dtype), C=r(b, 1, n, l).to(dtype),
+             A=-torch.arange(1, n + 1, device="cuda", dtype=torch.float32).repeat(d, 1),
+             D=1 + 0.1 * r(d), delta_bias=torch.log(torch.expm1(torch.rand(d, device="cuda", generator=g) * 0.099 + 1e-3)),
+             dout=r(b, d, l).to(dtype))
+    if pq_rank:
+        t["P"], t["Q"] = 0.1 * r(n, pq_rank), 0.1 * r(pq_rank, n)
+    return t
+
+
+def _refk_bench(mod, t, pq, warmup, iters, do_bwd=True):
+    kw = dict(D=t["D"], z=t["z"], delta_bias=t["delta_bias"])
+    if pq:
+        kw.update(P=t["P"], Q=t["Q"])
+    args = (t["u"], t["delta"], t["A"], t["B"], t["C"])
+    fwd = lambda: mod.fwd(*args, delta_softplus=True, **kw)
+    ms_f = _time_median(fwd, warmup, iters)
+    ms_b = None
+    if do_bwd:
+        out, x, *_ = fwd()
+        dP = torch.zeros_like(t["P"]) if pq else None
+        dQ = torch.zeros_like(t["Q"]) if pq else None
+        bwd = lambda: mod.bwd(*args, dout=t["dout"], x=x, out=out if t["z"] is not None else None, dz=None,
+                              dP_out=dP, dQ_out=dQ, delta_softplus=True, recompute_out_z=False, **kw)
+        ms_b = _time_median(bwd, warmup, iters)
+    return ms_f, ms_b
+
+
+def run_refkernel(args):
+    """This library's selective-scan kernels beside the reference's own CUDA extension (built
+    from the reference's sources for sm_100a into oracle/_ref/ by oracle/build_ref_scan.py) on
+    the same device inputs; one JSON line per workload with both times and the ratio.
+
+    Workloads: BASELINE config 4 (32 x 3072 x L, n 16, bf16 I/O, z, D, delta_bias, softplus) at
+    L = 1024 and 4096 (``--quick``: 1024 only), fwd and bwd separately; the module's d_state 32
+    and 64 size presets at 8 x d_inner x 2048; the motif P/Q path (rank 4, shared P/Q, no z,
+    since the reference's P/Q backward has none) at sizes the reference's one-thread-per-row
+    kernels (forward O(L), backward O(L^2)) finish in seconds.  CUDA-event medians after
+    warm-up on the current stream; config-4 inputs are > 126 MB L2."""
+    if args.impl == "reference":
+        print(json.dumps({"impl": "reference", "unavailable": "refkernel already times the reference kernel "
+                          "beside ours in one run"}))
+        return 0
+    from oracle import build_ref_scan
+    ref = build_ref_scan.load()
+    if ref is None:
+        print(json.dumps({"unavailable": "reference extension not built (MOTIF_REF=... python oracle/build_ref_scan.py)"}))
+        return 0
+    from motif_ssm import selective_scan_cuda as ours
+    work = [("config4", 32, 3072, L, 16, torch.bfloat16, True, 0, True) for L in ((1024,) if args.quick else (1024, 4096))]
+    if not args.quick:
+        # the module's larger size presets (d_state 32 / 64, mamba_simplemotif.py:32-36), z on
+        work += [("small_n32", 8, 1024, 2048, 32, torch.bfloat16, True, 0, True),
+                 ("base_n64", 8, 1536, 2048, 64, torch.bfloat16, True, 0, True)]
+        work += [("pq_fwd", 8, 1536, 2048, 16, torch.bfloat16, False, 4, False),
+                 ("pq_fwd_bwd", 2, 1536, 256, 16, torch.bfloat16, False, 4, True)]
+    for name, b, d, l, n, dtype, z, r, do_bwd in work:
+        t = _refk_inputs(b, d, l, n, dtype, z=z, pq_rank=r)
+        iters = 3 if r else 10
+        of, ob = _refk_bench(ours, t, r > 0, 3, iters, do_bwd)
+        rf, rb = _refk_bench(ref, t, r > 0, 1 if r else 3, iters, do_bwd)
+        line = {"workload": name, "batch": b, "d_inner": d, "seqlen": l, "d_state": n, "dtype": str(dtype)[6:],
+                "z": z, "pq_rank": r, "ours_fwd_ms": of, "ref_fwd_ms": rf, "fwd_speedup": rf / of}
+        if do_bwd:
+            line.update(ours_bwd_ms=ob, ref_bwd_ms=rb, bwd_speedup=rb / ob)
+        print(json.dumps(line), flush=True)
+        del t
+        torch.cuda.empty_cache()
     return 0
 
 

@@ -204,8 +204,12 @@ MSS_API int ss_bwd_workspace_size(const ss_bwd_args *a, int64_t *bytes);
 MSS_API int ss_fwd(const ss_fwd_args *a, void *stream);
 /* selective scan backward: writes du, ddelta, dA, dB, dC, dD, ddelta_bias, dz, out_z.  (selective_scan.cpp:415-618) */
 MSS_API int ss_bwd(const ss_bwd_args *a, void *stream);
-/* Scratch bytes ss_bwd_noalloc owns per GPU (64 MiB: enough for batch x n_groups x dstate
- * x seqlen up to 8 Mi, e.g. 32 x 1 x 16 x 16384). */
+/* Scratch bytes ss_bwd_noalloc owns per GPU (64 MiB).  A call is accepted when
+ * ss_bwd_workspace_size() for its arguments is at most this.  For dstate <= 16 without P/Q
+ * that is the fp32 dB / dC accumulators, 2 x batch x n_groups x dstate x round_up(seqlen, 4)
+ * x 4 bytes (e.g. 32 x 1 x 16 x 16384 fits); dstate > 16 adds a per-step scratch of
+ * batch x dim x 2 x round_up(seqlen, 4) x 4 bytes and P/Q a checkpoint array that also
+ * grows with batch x dim x seqlen, so those calls reach the limit at much smaller sizes. */
 #define MSS_BWD_NOALLOC_SCRATCH_BYTES (64ll << 20)
 
 /* ss_bwd for callers that cannot allocate device memory: code whose device memory is owned
@@ -213,10 +217,13 @@ MSS_API int ss_bwd(const ss_bwd_args *a, void *stream);
  * that forbids cudaMalloc in its steady state because cudaMalloc can synchronize the device
  * and has no latency bound.  No counterpart in the reference.  Same arguments and results as ss_bwd,
  * but `workspace` / `workspace_bytes` are ignored: the scratch is a static device array of
- * MSS_BWD_NOALLOC_SCRATCH_BYTES that this library keeps on every GPU it is loaded on.
- * Sizes needing more scratch than that fail with MSS_ERR_WORKSPACE.  The first call on a
- * device looks the array's address up (make it before any stream capture); every call shares
- * the array, so calls that overlap on the GPU race.  It calls no allocator. */
+ * MSS_BWD_NOALLOC_SCRATCH_BYTES in this library's device image: it is placed on a GPU when
+ * the library's module is loaded there (at the latest on the first call on that device) and
+ * held until the process exits.  Sizes whose ss_bwd_workspace_size() exceeds it fail with
+ * MSS_ERR_WORKSPACE.  The first call on a device looks the array's address up and caches it
+ * per device (make that call before any stream capture; resetting the device afterwards,
+ * e.g. cudaDeviceReset, is not supported).  Every call shares the array, so calls that
+ * overlap on the GPU race.  It calls no allocator. */
 MSS_API int ss_bwd_noalloc(const ss_bwd_args *a, void *stream);
 
 /* depthwise causal conv1d (+SiLU) forward / backward (causal-conv1d API) */

@@ -5,19 +5,19 @@ The sources, flags and module name follow the reference's ``setup.py:211-263``
 (``csrc/selective_scan/selective_scan.cpp`` + the nine ``selective_scan_{fwd,bwd}_*.cu``
 instantiations, ``-O3 --use_fast_math`` and the half/bf16 operator flags); only the
 architecture is this machine's (``TORCH_CUDA_ARCH_LIST=10.0a``, i.e. sm_100a).  Nothing is
-copied into the repository: the build reads the files under ``$MOTIF_REF`` (default: the
-reference checkout) and writes ``oracle/_ref/selective_scan_cuda*.so``, which is git-ignored
+copied into the repository: the build reads the files under ``$MOTIF_REF`` (required: the
+reference checkout's ``motifmamba`` project directory) and writes ``oracle/_ref/selective_scan_cuda*.so``, which is git-ignored
 but travels with the working tree.  Used only by GPU tests (parity of this library against
-the reference kernel) and by ``tests/ref_kernel_timing.py``; the product never loads it.
+the reference kernel) and by ``bench.py --workload refkernel``; the product never loads it.
 
-    python oracle/build_ref_scan.py          # ~10 min with 4 nvcc threads per file
+    MOTIF_REF=<reference>/motifmamba python oracle/build_ref_scan.py   # ~10 min, 4 nvcc threads per file
 """
 import os
 import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "_ref")
-REF = os.environ.get("MOTIF_REF", "/root/reference/motifmamba")
+REF = os.environ.get("MOTIF_REF")  # the reference project directory; nothing is built without it
 SOURCES = ["selective_scan.cpp"] + [f"selective_scan_fwd_{t}.cu" for t in ("fp32", "fp16", "bf16")] + [
     f"selective_scan_bwd_{t}_{k}.cu" for t in ("fp32", "fp16", "bf16") for k in ("real", "complex")]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-U__CUDA_NO_HALF_OPERATORS__", "-U__CUDA_NO_HALF_CONVERSIONS__",
@@ -53,6 +53,8 @@ def load():
 
 
 def build():
+    if not REF:
+        raise SystemExit("set MOTIF_REF to the reference's motifmamba project directory")
     src_dir = os.path.join(REF, "csrc", "selective_scan")
     if not os.path.isdir(src_dir):
         print(f"reference sources not found under {src_dir}; nothing built")

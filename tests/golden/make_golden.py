@@ -16,7 +16,7 @@ before the file is executed:
 ``motifmamba/mamba_ssm/modules/mamba_simplemotif.py:75-83, 295``).
 
 Run in a container that has the reference checkout (its ``motifmamba`` project directory
-in ``$MOTIF_REF``, default the checkout's usual location below).  The outputs are small
+in ``$MOTIF_REF``, which is required).  The outputs are small
 ``.pt`` files next to this script; nothing at test time reads the reference.
 """
 import importlib.util
@@ -28,7 +28,9 @@ import torch
 import torch.nn.functional as F
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("MOTIF_REF", "/root/reference/motifmamba")
+REF = os.environ.get("MOTIF_REF")
+if not REF:
+    raise SystemExit("set MOTIF_REF to the reference's motifmamba project directory")
 
 
 def _stub(name, **attrs):

@@ -44,9 +44,9 @@ def test_causal_conv1d_fwd_bwd(batch, dim, seqlen, width, dtype, wdtype, bias, s
     t = tol(dtype)
     assert_close(out, ref, t, t, "conv out")
     assert_close(dl[0].grad, leaves[0].grad, t, t, "conv dx")
-    assert_close(dl[1].grad, leaves[1].grad, t, t, "conv dweight")
+    assert_close(dl[1].grad, leaves[1].grad, t, t, "conv dweight", scaled=True)
     if bias:
-        assert_close(dl[2].grad, leaves[2].grad, t, t, "conv dbias")
+        assert_close(dl[2].grad, leaves[2].grad, t, t, "conv dbias", scaled=True)
 
 
 @pytest.mark.parametrize("state_len,width,dtype,sdtype", [
@@ -168,7 +168,7 @@ def test_mamba_inner_matches_reference_golden():
     out.backward(rec["dout"].to(DEV))
     assert_close(out, rec["out"], 1e-3, 1e-3, "inner out")
     for k, g in rec["grads"].items():
-        assert_close(leaves[k].grad, g, 1e-3, 1e-3, f"inner d{k}")
+        assert_close(leaves[k].grad, g, 1e-3, 1e-3, f"inner d{k}", scaled=k != "xz")
 
 
 def test_mamba_inner_bf16_config1_block_vs_oracle():
@@ -232,7 +232,7 @@ def test_mamba_inner_rms_options(which, checkpoint_lvl):
             ref.backward(rec["dout"])
             out.backward(rec["dout"].to(DEV))
             for k in inp:
-                assert_close(dl[k].grad, leaves[k].grad, 1e-3, 1e-3, f"{which} d{k}")
+                assert_close(dl[k].grad, leaves[k].grad, 1e-3, 1e-3, f"{which} d{k}", scaled=k != "xz")
 
 
 @pytest.mark.parametrize("dtype,rdtype,with_res", [(torch.bfloat16, torch.float32, True),
@@ -264,7 +264,7 @@ def test_add_rms_norm_fused(dtype, rdtype, with_res):
     assert_close(leaves[0].grad, ref_leaves[0].grad, t, t, "dx")
     if with_res:
         assert_close(leaves[1].grad, ref_leaves[1].grad, t, t, "dresidual")
-    assert_close(leaves[2].grad, ref_leaves[2].grad, t, t, "dweight")
+    assert_close(leaves[2].grad, ref_leaves[2].grad, t, t, "dweight", scaled=True)
 
 
 def test_layer_norm_module_stand_in():

@@ -2,8 +2,9 @@
 with the golden fixtures produced by the reference's own code.
 
 Tolerances (north star): outputs, last_state and the 8 gradients within 1e-3 for fp32
-I/O and 2e-2 for bf16/fp16 I/O, relative to the tensor's magnitude (see
-``ssm_cases.assert_close``)."""
+I/O and 2e-2 for bf16/fp16 I/O, elementwise (|a - e| <= atol + rtol |e|) for
+outputs, last_state, du, ddelta and dz; sums over channels / batch (dA, dB, dC, dD,
+ddelta_bias) relative to the tensor's magnitude (see ``ssm_cases.assert_close``)."""
 import glob
 import os
 
@@ -11,7 +12,7 @@ import pytest
 import torch
 
 from oracle import ssm_oracle as O
-from ssm_cases import assert_close, make_scan_inputs, tol
+from ssm_cases import SUM_GRADS, assert_close, make_scan_inputs, tol
 
 pytestmark = pytest.mark.gpu
 GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
@@ -46,7 +47,7 @@ def compare(out, last, grads, ref_out, ref_last, ref_grads, dtype, what=""):
                 assert grads[k] is None, k
                 continue
             assert grads[k] is not None, k
-            assert_close(grads[k], ref_grads[k], t, t, f"{what} d{k}")
+            assert_close(grads[k], ref_grads[k], t, t, f"{what} d{k}", scaled=k in SUM_GRADS)
 
 
 def oracle(inputs, dout, softplus):
@@ -154,11 +155,11 @@ def test_scan_full_size_rows_and_linearity():
     assert_close(gu[bsel:bsel + 1, dsel], r_g["u"], t, t, "du rows")
     assert_close(gdelta[bsel:bsel + 1, dsel], r_g["delta"], t, t, "ddelta rows")
     assert_close(gz[bsel:bsel + 1, dsel], r_g["z"], t, t, "dz rows")
-    assert_close(gA[dsel], r_g["A"], t, t, "dA rows")
-    assert_close(gD[dsel], r_g["D"], t, t, "dD rows")
-    assert_close(gbias[dsel], r_g["delta_bias"], t, t, "ddelta_bias rows")
-    assert_close(gB[bsel:bsel + 1], r_g["B"], t, t, "dB (sum over channels)")
-    assert_close(gC[bsel:bsel + 1], r_g["C"], t, t, "dC (sum over channels)")
+    assert_close(gA[dsel], r_g["A"], t, t, "dA rows", scaled=True)
+    assert_close(gD[dsel], r_g["D"], t, t, "dD rows", scaled=True)
+    assert_close(gbias[dsel], r_g["delta_bias"], t, t, "ddelta_bias rows", scaled=True)
+    assert_close(gB[bsel:bsel + 1], r_g["B"], t, t, "dB (sum over channels)", scaled=True)
+    assert_close(gC[bsel:bsel + 1], r_g["C"], t, t, "dC (sum over channels)", scaled=True)
     # every other row got no gradient
     mask = torch.ones(batch, dim, dtype=torch.bool, device=DEV)
     mask[bsel, dsel] = False
