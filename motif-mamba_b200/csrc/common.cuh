@@ -124,6 +124,15 @@ __device__ __forceinline__ float softplus20(float x) {
     const float r = y < 0.0625f ? small : big;
     return x <= 20.f ? r : x;
 }
+// softplus'(x) = sigmoid(x) = 1 - e^(-s) from the softplus output s = softplus(x) >= 0.  For
+// s < 1/16 the difference 1 - e^(-s) would cancel (and be 0 once e^(-s) rounds to 1, i.e. for
+// x below about -16), so the series s - s^2/2 + s^3/6 - s^4/24 is used there (truncation
+// < s^5/120, i.e. < 2e-7 relative).
+__device__ __forceinline__ float softplus_grad_from_out(float s) {
+    const float big = 1.f - ex2(-s * kLog2e);
+    const float small = s * fmaf(s, fmaf(s, fmaf(s, -1.f / 24.f, 1.f / 6.f), -0.5f), 1.f);
+    return s < 0.0625f ? small : big;
+}
 // 1 / (1 + e^-x) with the SFU exponential and a fast reciprocal (relative error ~1e-7).
 __device__ __forceinline__ float sigmoidf_(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
 

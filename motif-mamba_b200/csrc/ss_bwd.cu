@@ -519,7 +519,7 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
                         const float S1v = h ? s1.y : s1.x, S2v = h ? s2.y : s2.x, dtv = h ? df.y : df.x;
                         const float dgv = h ? dg.y : dg.x, uv = h ? u.y : u.x;
                         // softplus'(x) = sigmoid(x) = 1 - exp(-softplus(x)); 1 above the threshold
-                        const float gate = p.softplus ? (dtv > 20.f ? 1.f : 1.f - ex2(-dtv * kLog2e)) : 1.f;
+                        const float gate = p.softplus ? (dtv > 20.f ? 1.f : softplus_grad_from_out(dtv)) : 1.f;
                         du[i] = fmaf(dtv, S1v, Dv * dgv);
                         dd[i] = fmaf(uv, S1v, S2v) * gate;
                         if (t0 + i < L) {

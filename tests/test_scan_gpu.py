@@ -12,7 +12,7 @@ import pytest
 import torch
 
 from oracle import ssm_oracle as O
-from ssm_cases import SUM_GRADS, assert_close, make_scan_inputs, tol
+from ssm_cases import SUM_GRADS, assert_close, make_scan_inputs, oracle_fp32_math, tol
 
 pytestmark = pytest.mark.gpu
 GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
@@ -51,8 +51,7 @@ def compare(out, last, grads, ref_out, ref_last, ref_grads, dtype, what=""):
 
 
 def oracle(inputs, dout, softplus):
-    cpu = {k: (v.cpu() if v is not None else None) for k, v in inputs.items()}
-    return O.scan_with_grads(cpu, dout.cpu(), softplus)
+    return oracle_fp32_math(inputs, dout, softplus)
 
 
 @pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(GOLD, "scan_*.pt"))),
@@ -147,7 +146,7 @@ def test_scan_full_size_rows_and_linearity():
     sub = dict(u=cpu(u[bsel:bsel + 1, dsel]), delta=cpu(delta[bsel:bsel + 1, dsel]), A=cpu(A[dsel]),
                B=cpu(B[bsel:bsel + 1]), C=cpu(C[bsel:bsel + 1]), D=cpu(D[dsel]), z=cpu(z[bsel:bsel + 1, dsel]),
                delta_bias=cpu(bias[dsel]))
-    r_out, r_last, r_g = O.scan_with_grads(sub, cpu(dout[bsel:bsel + 1, dsel]), True)
+    r_out, r_last, r_g = oracle_fp32_math(sub, cpu(dout[bsel:bsel + 1, dsel]), True)
     t = 2e-2
     assert_close(out[bsel:bsel + 1, dsel], r_out, t, t, "full-size out rows")
     assert_close(last[bsel:bsel + 1, dsel], r_last, t, t, "full-size last_state rows")
