@@ -255,9 +255,13 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true", help="scan workload: skip the config-2 prefill sub-record")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the per-GPU batch (profiling a smaller case of the same kernels)")
     ap.add_argument("--seqlen", type=int, default=None, help="override the sequence length")
+    ap.add_argument("--global-batch", type=int, default=None,
+                    help="prefill workload: override the global batch (e.g. 2 = one GPU's share at 8 GPUs)")
+    ap.add_argument("--no-decode", action="store_true", help="prefill workload: skip the decode measurement")
     ap.add_argument("--once", action="store_true", help="kernels workload: run each kernel twice (ncu capture)")
     ap.add_argument("--quick", action="store_true", help="refkernel workload: config 4 at seqlen 1024 only")
     ap.add_argument("--workload", default="scan", choices=["scan", "prefill", "tp", "pq", "kernels", "refkernel"],
@@ -270,6 +274,8 @@ def main():
     args = ap.parse_args()
     if args.batch:
         CFG["batch"] = args.batch
+    if args.global_batch:
+        PREFILL["global_batch"] = args.global_batch
     if args.seqlen:
         CFG["seqlen"] = args.seqlen
     args.warmup = max(args.warmup, 3)
@@ -346,6 +352,16 @@ def main():
         e2e = run_e2e(t, dout, dev, stream, world, selective_scan_fn, fwd_b + bwd_b, max(3, args.steps // 4),
                       dist if world > 1 else None)
 
+    # ---- config-2 prefill (strong scaling over the ranks) and, at world > 1, the TP parity check ----
+    prefill = None
+    if not args.no_prefill:
+        del t, dout
+        torch.cuda.empty_cache()
+        pre_args = argparse.Namespace(steps=max(3, min(args.steps, 10)), warmup=args.warmup)
+        prefill, pre_clocks = measure_prefill(pre_args, world, rank, local, dev, with_decode=False, with_e2e=False)
+        prefill["clocks"] = pre_clocks
+    tpc = tp_check(world, rank, dev) if world > 1 else None
+
     peak, peak_kind = hbm_peak()
     dom_ms, dom_bytes, dom_name = (bwd_ms, bwd_b, "ss_bwd") if bwd_ms >= fwd_ms else (fwd_ms, fwd_b, "ss_fwd")
     achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
@@ -376,11 +392,47 @@ def main():
             "clocks": clocks,
             "e2e": e2e,
             "cpu_baseline": cpu,
+            "prefill": prefill,
+            "tp_check": tpc,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
     return 0
+
+
+def tp_check(world, rank, dev, seqlen=1024, n_layer=2):
+    """Parity of the channel-sharded TP path at this world size: a config-3-shaped stack
+    (d_model 2560, d_inner 5120, n 16, dt_rank 160; 2 layers, vocab 512), bf16 random init
+    with the same seed on every rank, 1 x 1024 random ids.  Rank 0 runs the unsharded model
+    first; then every rank shards it (shard_model_tp: x_proj partial sums all-reduced in fp32,
+    out_proj partial sums in bf16 over NCCL) and the sharded logits are compared with the
+    unsharded ones on rank 0: |a - e| <= 2e-2 + 2e-2 |e| elementwise."""
+    import torch.distributed as dist
+    from motif_ssm.modules import MambaConfig, MambaLMHeadModel, shard_model_tp
+    torch.manual_seed(0)
+    model = MambaLMHeadModel(MambaConfig(d_model=2560, n_layer=n_layer, vocab_size=512, ssm_cfg={"d_state": 16}),
+                             device=dev, dtype=torch.bfloat16)
+    model.eval()
+    ids = torch.randint(0, 512, (1, seqlen), device=dev, generator=torch.Generator(device=dev).manual_seed(7))
+    ref = None
+    with torch.no_grad():
+        if rank == 0:
+            ref = model(ids).float()
+        shard_model_tp(model, rank, world)
+        out = model(ids).float()
+    torch.cuda.synchronize()
+    res = None
+    if rank == 0:
+        err = (out - ref).abs()
+        bound = 2e-2 + 2e-2 * ref.abs()
+        res = {"world": world, "layers": n_layer, "tokens": seqlen, "max_abs_err": err.max().item(),
+               "max_ref": ref.abs().max().item(), "violations": int((err > bound).sum().item()),
+               "pass": bool((err <= bound).all().item())}
+    del model
+    torch.cuda.empty_cache()
+    dist.barrier()
+    return res
 
 
 def ssc_needs_split():
@@ -522,11 +574,96 @@ def _cpu_prefill_tok_s(threads, seqlen=512):
                        f"oracle restatement of mamba_inner_ref in fp32: {dt:.2f} s, extrapolated to 24 layers")
 
 
+def measure_prefill(args, world, rank, local, dev, with_decode=True, with_e2e=True):
+    """Config 2: 24-layer MotifMamba stack, bf16 random init, vocab 512 random ids.  Prefill of
+    a fixed global batch of 16 x 4096 split over ranks (strong scaling; no collective: each rank
+    runs its own rows), timed with CUDA events, max over ranks; optionally 256 greedy decode
+    steps at global batch 64 through the cache and an end-to-end number (host ids in, last-token
+    logits out).  Returns the record (every rank), the clock samples of the timed region."""
+    import torch.distributed as dist
+    from motif_ssm.modules import GraphedForward, InferenceParams, MambaConfig, MambaLMHeadModel
+    P = PREFILL
+    torch.manual_seed(0)
+    model = MambaLMHeadModel(MambaConfig(d_model=P["d_model"], n_layer=P["n_layer"], vocab_size=P["vocab"],
+                                         ssm_cfg={"d_state": P["d_state"]}), device=dev, dtype=torch.bfloat16)
+    model.eval()
+    bl = max(1, P["global_batch"] // world)
+    g = torch.Generator(device=dev).manual_seed(rank)
+    ids = torch.randint(0, P["vocab"], (bl, P["seqlen"]), device=dev, generator=g)
+    stream = torch.cuda.current_stream(dev)
+    graphed = GraphedForward(model, bl, P["seqlen"])  # the whole prefill as one CUDA graph
+
+    for _ in range(args.warmup):
+        graphed(ids)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        s.record(stream)
+        for _ in range(args.steps):
+            graphed(ids)
+        e.record(stream)
+        torch.cuda.synchronize()
+    tt = torch.tensor([s.elapsed_time(e) / args.steps], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    ms = tt.item()
+    rec = {"metric": "MotifMamba prefill tok/s (config 2)", "value": bl * world * P["seqlen"] / (ms * 1e-3),
+           "unit": "tok/s", "ms_per_step": ms, "n_gpus": world, "scaling": "strong",
+           "config": {"workload": "24-layer MotifMamba stack (d_model 768, d_inner 1536, n 16, RMSNorm, vocab 512), "
+                                  "bf16 random init, prefill of global batch 16 x 4096 random ids, last-token logits",
+                      "global_batch": bl * world, "batch_per_gpu": bl, "seqlen": P["seqlen"],
+                      "parallelism": f"batch-sharded x{world}", "cuda_graph": True}}
+    clocks = clk.summary()
+
+    if with_decode:  # greedy decode through the cache
+        db = max(1, P["decode_batch"] // world)
+        prompt = torch.randint(0, P["vocab"], (db, P["prompt"]), device=dev, generator=g)
+        with torch.no_grad():
+            params = InferenceParams(max_seqlen=P["prompt"] + P["decode_steps"], max_batch_size=db)
+            tok = model(prompt, inference_params=params, num_last_tokens=1).argmax(-1)
+            params.seqlen_offset = P["prompt"]
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            from motif_ssm.modules import GraphedDecoder
+            dec = GraphedDecoder(model, params, db)   # whole decode step as one CUDA graph
+            s.record(stream)
+            for _ in range(P["decode_steps"]):
+                tok = dec.step(tok).argmax(-1)
+            e.record(stream)
+            torch.cuda.synchronize()
+        td = torch.tensor([s.elapsed_time(e)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(td, op=dist.ReduceOp.MAX)
+        rec["decode_tok_s"] = db * world * P["decode_steps"] / (td.item() * 1e-3)
+        rec["decode"] = {"global_batch": db * world, "steps": P["decode_steps"], "prompt": P["prompt"],
+                         "cuda_graph": True}
+
+    if with_e2e:  # end to end: host ids in, last-token logits out
+        host_ids = ids.cpu().pin_memory()
+        dev_ids = torch.empty_like(ids)
+        out_host = torch.empty((bl, 1, model.lm_head.weight.shape[0]), dtype=torch.bfloat16).pin_memory()
+        s.record(stream)
+        for _ in range(args.steps):
+            dev_ids.copy_(host_ids, non_blocking=True)
+            lg = graphed(dev_ids)
+            out_host.copy_(lg, non_blocking=True)
+        e.record(stream)
+        torch.cuda.synchronize()
+        te = torch.tensor([s.elapsed_time(e) / args.steps], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        rec["e2e"] = {"value": bl * world * P["seqlen"] / (te.item() * 1e-3), "unit": "tok/s",
+                      "h2d_bytes_per_step": host_ids.numel() * 8, "d2h_bytes_per_step": out_host.numel() * 2}
+    del graphed, model
+    torch.cuda.empty_cache()
+    return rec, clocks
+
+
 def run_prefill(args):
-    """Config 2: 24-layer MotifMamba stack, bf16 random init, vocab 512 random ids.
-    Prefill of a fixed global batch of 16 x 4096 split over ranks (strong scaling; no
-    collective: each rank runs its own rows), then 256 greedy decode steps at global
-    batch 64 through the cache (conv / state update kernels)."""
+    """--workload prefill: the config-2 prefill record as the headline line."""
     import torch.distributed as dist
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -545,97 +682,14 @@ def run_prefill(args):
     dev = torch.device("cuda", local)
     if world > 1:
         dist.init_process_group("nccl", device_id=dev)
-    from motif_ssm.modules import InferenceParams, MambaConfig, MambaLMHeadModel
-    P = PREFILL
-    torch.manual_seed(0)
-    model = MambaLMHeadModel(MambaConfig(d_model=P["d_model"], n_layer=P["n_layer"], vocab_size=P["vocab"],
-                                         ssm_cfg={"d_state": P["d_state"]}), device=dev, dtype=torch.bfloat16)
-    model.eval()
-    bl = max(1, P["global_batch"] // world)
-    g = torch.Generator(device=dev).manual_seed(rank)
-    ids = torch.randint(0, P["vocab"], (bl, P["seqlen"]), device=dev, generator=g)
-    stream = torch.cuda.current_stream(dev)
-    from motif_ssm.modules import GraphedForward
-    graphed = GraphedForward(model, bl, P["seqlen"])  # the whole prefill as one CUDA graph
-
-    def prefill():
-        return graphed(ids)
-
-    for _ in range(args.warmup):
-        prefill()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        s.record(stream)
-        for _ in range(args.steps):
-            prefill()
-        e.record(stream)
-        torch.cuda.synchronize()
-    tt = torch.tensor([s.elapsed_time(e) / args.steps], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-    ms = tt.item()
-    value = bl * world * P["seqlen"] / (ms * 1e-3)
-
-    # greedy decode through the cache
-    db = max(1, P["decode_batch"] // world)
-    prompt = torch.randint(0, P["vocab"], (db, P["prompt"]), device=dev, generator=g)
-    with torch.no_grad():
-        params = InferenceParams(max_seqlen=P["prompt"] + P["decode_steps"], max_batch_size=db)
-        tok = model(prompt, inference_params=params, num_last_tokens=1).argmax(-1)
-        params.seqlen_offset = P["prompt"]
-        for _ in range(3):  # warm-up steps on a copy of the cache
-            model(tok, inference_params=InferenceParams(max_seqlen=8, max_batch_size=db,
-                                                         seqlen_offset=1,
-                                                         key_value_memory_dict={k: (a.clone(), b.clone()) for k, (a, b) in params.key_value_memory_dict.items()}),
-                  num_last_tokens=1)
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        from motif_ssm.modules import GraphedDecoder
-        dec = GraphedDecoder(model, params, db)   # whole decode step as one CUDA graph
-        s.record(stream)
-        for _ in range(P["decode_steps"]):
-            tok = dec.step(tok).argmax(-1)
-        e.record(stream)
-        torch.cuda.synchronize()
-    td = torch.tensor([s.elapsed_time(e)], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(td, op=dist.ReduceOp.MAX)
-    decode_tok_s = db * world * P["decode_steps"] / (td.item() * 1e-3)
-
-    # end to end: host ids in, last-token logits out
-    host_ids = ids.cpu().pin_memory()
-    dev_ids = torch.empty_like(ids)
-    out_host = torch.empty((bl, 1, model.lm_head.weight.shape[0]), dtype=torch.bfloat16).pin_memory()
-    s.record(stream)
-    for _ in range(args.steps):
-        dev_ids.copy_(host_ids, non_blocking=True)
-        lg = graphed(dev_ids)
-        out_host.copy_(lg, non_blocking=True)
-    e.record(stream)
-    torch.cuda.synchronize()
-    te = torch.tensor([s.elapsed_time(e) / args.steps], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    rec, clocks = measure_prefill(args, world, rank, local, dev, with_decode=not args.no_decode)
     cpu = _cpu_prefill_tok_s(cpu_threads()) if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
     if rank == 0:
-        print(json.dumps({
-            "metric": "MotifMamba prefill tok/s (config 2)", "value": value, "unit": "tok/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "24-layer MotifMamba stack (d_model 768, d_inner 1536, n 16, RMSNorm, vocab 512), "
-                                   "bf16 random init, prefill of global batch 16 x 4096 random ids, last-token logits",
-                       "global_batch": bl * world, "seqlen": P["seqlen"], "parallelism": f"batch-sharded x{world}",
-                       "cuda_graph": True},
-            "decode_tok_s": decode_tok_s, "decode": {"global_batch": db * world, "steps": P["decode_steps"],
-                                                     "prompt": P["prompt"], "cuda_graph": True},
-            "gpu_launches": None, "clocks": clk.summary(),
-            "e2e": {"value": bl * world * P["seqlen"] / (te.item() * 1e-3), "unit": "tok/s",
-                    "h2d_bytes_per_step": host_ids.numel() * 8, "d2h_bytes_per_step": out_host.numel() * 2},
-            "cpu_baseline": cpu}), flush=True)
+        line = dict(rec)
+        line.update({"steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "vs_baseline": None,
+                     "dtype": "bf16", "data": "synthetic", "gpu_launches": None, "clocks": clocks,
+                     "cpu_baseline": cpu})
+        print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
     return 0

@@ -19,10 +19,11 @@
 // thread reads with broadcast 16-byte loads.  Outputs are written in place into the
 // staged u / z rows and leave through coalesced 16-byte stores.
 //
-// When batch * dim is too small to fill 148 SMs, the sequence is split into S segments
-// (a multiple of kChunkLen long): a carry pass computes each segment's end state from
-// zero and its summed dt, then the main pass folds the carries of earlier segments into
-// its initial state (h_in = prod(decay) * h_in + H) and runs the full scan.
+// When batch * dim is too small to fill 148 SMs, the sequence is split into up to 32
+// segments (whole 16-step tiles): a carry pass computes each segment's end state from zero
+// and its summed dt, a shuffle scan over segments (seg_carry_scan_kernel) composes them into
+// every segment's initial state (h_in = prod(decay) * h_in + H), and the main pass runs the
+// full scan of each segment from its initial state.
 #include <type_traits>
 
 #include "common.cuh"
@@ -147,30 +148,12 @@ __global__ void __launch_bounds__(FwdCfg<NS, SPT>::NT, FwdCfg<NS, SPT>::MINB) ss
     float cum = 0.f;  // sum of dt since t = 0 (main pass) or since the segment start (carry pass)
     const int64_t row = (int64_t)b * p.dim + d;
     if (!CARRY && s > 0 && valid) {
-        // fold the carries of the earlier segments: h = decay(segment) h + H(segment)
-        for (int sp = 0; sp < s; ++sp) {
-            const float dts = p.ws_dts[row * p.n_seg + sp];
-            const float *H = p.ws_h + (row * p.n_seg + sp) * NS + n0;
-            if (chain) {  // decay of state n over the segment = R^(n+1), R = exp(A_0 dts)
-                const float R = ex2(A2r * dts);
-                float pw = LPC == 1 ? R : ex2(A2[0] * dts);  // R^(n0 + 1)
+        // initial state of this segment and the summed dt before it, left in the workspace by
+        // seg_carry_scan_kernel (the carries of the earlier segments composed in log depth)
+        const float *H = p.ws_h + (row * p.n_seg + s) * NS + n0;
 #pragma unroll
-                for (int m = 0; m < NP; ++m) {
-                    const float2 hv = unpack2(h2[m]);
-                    const float p0 = pw, p1 = pw * R;
-                    pw = p1 * R;
-                    h2[m] = pack2(fmaf(p0, hv.x, H[2 * m]), fmaf(p1, hv.y, H[2 * m + 1]));
-                }
-            } else {
-#pragma unroll
-                for (int m = 0; m < NP; ++m) {
-                    const float2 hv = unpack2(h2[m]);
-                    h2[m] = pack2(fmaf(ex2(A2[2 * m] * dts), hv.x, H[2 * m]),
-                                  fmaf(ex2(A2[2 * m + 1] * dts), hv.y, H[2 * m + 1]));
-                }
-            }
-            cum += dts;
-        }
+        for (int m = 0; m < NP; ++m) h2[m] = pack2(H[2 * m], H[2 * m + 1]);
+        cum = p.ws_dts[row * p.n_seg + s];
     }
 
     const T *gu = reinterpret_cast<const T *>(p.u) + (int64_t)b * p.u_bs + (int64_t)c0 * p.u_ds;
@@ -320,6 +303,50 @@ __global__ void __launch_bounds__(FwdCfg<NS, SPT>::NT, FwdCfg<NS, SPT>::MINB) ss
     }
 }
 
+// Turns the per-segment carries into per-segment initial states.  On entry, for every row and
+// segment s < n_seg - 1, ws_h[row][s][n] holds H_s[n], the state at the end of segment s started
+// from zero, and ws_dts[row][s] the summed dt over it; segment s's decay of state n is
+// exp(A_n * dts_s).  On exit, slot s + 1 holds the state at the start of segment s + 1 (the
+// composition (D, H) o (D', H') = (D D', D' H + H') over segments 0..s) and ws_dts slot s + 1
+// the summed dt before it.  G lanes (a power of two >= n_seg - 1, <= 32) per (row, state), one
+// lane per segment, a log2(G)-level shuffle scan: latency O(log n_seg) instead of a chain of
+// dependent loads per segment in the main pass.
+__global__ void __launch_bounds__(256) seg_carry_scan_kernel(float *__restrict__ ws_h, float *__restrict__ ws_dts,
+                                                             const float *__restrict__ A, int64_t A_ds, int64_t A_ns,
+                                                             int64_t rows, int dim, int dstate, int ns, int n_seg,
+                                                             int G) {
+    const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int lane = threadIdx.x & (G - 1);          // segment
+    const int64_t pair = tid / G;                     // (row, state)
+    const bool in = pair < rows * ns;
+    const int64_t row = in ? pair / ns : 0;
+    const int n = in ? (int)(pair - row * ns) : 0;
+    const int d = (int)(row % dim);
+    const bool live = in && lane < n_seg - 1;         // segments that have a carry
+    const float a2 = (in && n < dstate) ? A[(int64_t)d * A_ds + (int64_t)n * A_ns] * kLog2e : 0.f;
+    float H = 0.f, dts = 0.f;
+    if (live) {
+        H = ws_h[(row * n_seg + lane) * ns + n];
+        dts = ws_dts[row * n_seg + lane];
+    }
+    // inclusive scan over the group's lanes: (Dl, Hl) composite of segments 0..lane; Sl = summed dt
+    float Dl = live ? ex2(a2 * dts) : 1.f, Hl = H, Sl = dts;
+    for (int off = 1; off < G; off <<= 1) {
+        const float Dp = __shfl_up_sync(0xffffffffu, Dl, off, G);
+        const float Hp = __shfl_up_sync(0xffffffffu, Hl, off, G);
+        const float Sp = __shfl_up_sync(0xffffffffu, Sl, off, G);
+        if (lane >= off) {
+            Hl = fmaf(Dl, Hp, Hl);
+            Dl *= Dp;
+            Sl += Sp;
+        }
+    }
+    if (live) {
+        ws_h[(row * n_seg + lane + 1) * ns + n] = Hl;
+        if (n == 0) ws_dts[row * n_seg + lane + 1] = Sl;
+    }
+}
+
 template <typename T, int NS, int SPT, bool HAS_Z, bool CARRY>
 static cudaError_t launch_one(const FwdParams &p, dim3 grid, cudaStream_t st) {
     using Ly = FwdLayout<T, NS, SPT, HAS_Z, CARRY>;
@@ -342,6 +369,13 @@ static cudaError_t launch_spt(FwdParams p, bool has_z, cudaStream_t st) {
     if (p.n_seg > 1) {
         dim3 gc(grid.x, p.n_seg - 1, grid.z);
         e = launch_one<T, NS, SPT, false, true>(p, gc, st);
+        if (e != cudaSuccess) return e;
+        int G = 2;
+        while (G < p.n_seg - 1) G <<= 1;  // n_seg <= 33 (abi.cu caps it at 32)
+        const int64_t threads = (int64_t)p.batch * p.dim * NS * G;
+        seg_carry_scan_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
+            p.ws_h, p.ws_dts, p.A, p.A_ds, p.A_ns, (int64_t)p.batch * p.dim, p.dim, p.dstate, NS, p.n_seg, G);
+        e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
     if (has_z) return launch_one<T, NS, SPT, true, false>(p, grid, st);

@@ -473,8 +473,14 @@ class TPMambamotif(nn.Module):
         xz = (self.in_proj_w @ hidden_states.reshape(-1, self.d_model).t()).view(-1, batch, seqlen).transpose(0, 1)
         x, z = xz.chunk(2, dim=1)
         x = causal_conv1d_fn(x, self.conv_w, self.conv_b, activation="silu")
-        x_dbl = x.transpose(1, 2).reshape(-1, self.d_local) @ self.x_proj_w.t()
-        x_dbl = self._all_reduce(x_dbl.contiguous())                       # all-reduce #1
+        # x_proj partial sums stay fp32 through the all-reduce and are rounded once, as the
+        # unsharded GEMM rounds its fp32 accumulator once
+        xt = x.transpose(1, 2).reshape(-1, self.d_local)
+        if xt.dtype in (torch.bfloat16, torch.float16):
+            x_dbl = torch.mm(xt, self.x_proj_w.t(), out_dtype=torch.float32)
+        else:
+            x_dbl = xt @ self.x_proj_w.t()
+        x_dbl = self._all_reduce(x_dbl.contiguous()).to(x.dtype)            # all-reduce #1
         dt, B, C = torch.split(x_dbl, [self.dt_rank, self.d_state, self.d_state], dim=-1)
         dt = (self.dt_proj_w @ dt.t()).view(self.d_local, batch, seqlen).transpose(0, 1)
         B = B.reshape(batch, seqlen, -1).transpose(1, 2).contiguous()
