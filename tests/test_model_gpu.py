@@ -91,6 +91,22 @@ def test_lm_stack_fp32_matches_oracle_stack():
     assert_close(logits, ref, 1e-3, 1e-3, "LM logits")
 
 
+def test_lm_stack_config2_24_layers_bf16_matches_oracle_stack():
+    """BASELINE config 2's stack (24 layers, d_model 768, d_inner 1536, n 16, RMSNorm, vocab
+    512) in bf16 with its random init, on a short slice (2 x 128 random ids): logits against
+    the oracle stack evaluated in fp32 on the same bf16 weights, at the bf16 tolerance."""
+    from motif_ssm.modules import MambaConfig, MambaLMHeadModel
+    torch.manual_seed(0)
+    cfg = MambaConfig(d_model=768, n_layer=24, vocab_size=512, ssm_cfg={"d_state": 16})
+    model = MambaLMHeadModel(cfg, device=DEV, dtype=torch.bfloat16)
+    model.eval()
+    ids = torch.randint(0, 512, (2, 128), device=DEV, generator=torch.Generator(device=DEV).manual_seed(3))
+    with torch.no_grad():
+        logits = model(ids)
+    ref = _stack_oracle(model, ids)
+    assert_close(logits, ref, 2e-2, 2e-2, "24-layer bf16 LM logits")
+
+
 def test_lm_greedy_decode_matches_full_prefill():
     """Decoding token by token through the cache gives the logits a full prefill gives."""
     from motif_ssm.modules import InferenceParams, MambaConfig, MambaLMHeadModel
