@@ -44,12 +44,12 @@ static_assert(CK == 32 * IT, "a warp covers one chunk");
 
 // Lane-interleaved chunk layout: timestep t = 8 l + 4 h + j (lane l, half h, j < 4) lives at
 // h * 128 + 4 l + j, so each lane reads its 8 steps as two conflict-free 16-byte loads.
-// 16-bit inputs keep B / C in their own type here (converted when read), which leaves room
-// for the per-warp prefetch buffers of the next pass's per-step inputs.
+// B / C are converted to fp32 once per chunk when staged (each value is then read by all
+// 8 K channels of the CTA), and 16-bit inputs get per-warp prefetch buffers for the next
+// pass's per-step inputs.
 template <typename T> struct BwdSmemT {
     static constexpr bool kPrefetch = sizeof(T) == 2;
-    using BCT = typename std::conditional<kPrefetch, T, float>::type;
-    BCT BC[2][bwd::NS][bwd::CK];              // B, C of the chunk
+    float BC[2][bwd::NS][bwd::CK];            // B, C of the chunk (fp32)
     float ACC[2][bwd::NS][bwd::CK];           // chunk accumulator of dB / dC
     float DHC[bwd::KMAX][bwd::W][bwd::NS];    // reverse-recurrence carry into the previous chunk
     float DAACC[bwd::KMAX][bwd::W][bwd::NS];  // dA accumulators
@@ -84,30 +84,27 @@ __device__ __forceinline__ void ld8(const float *base, int lane, float (&v)[8]) 
     v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
     v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
 }
-template <typename T> __device__ __forceinline__ void bc_ld8(const T *base, int lane, float (&v)[8]) {
-    // 16-bit layout: 4 values at [4 lane, 4 lane + 4) and 4 at [128 + 4 lane, ...)
-    const uint2 a = *reinterpret_cast<const uint2 *>(base + lane * 4);
-    const uint2 c = *reinterpret_cast<const uint2 *>(base + 128 + lane * 4);
-    const T *pa = reinterpret_cast<const T *>(&a), *pc = reinterpret_cast<const T *>(&c);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        v[j] = to_f<T>(pa[j]);
-        v[4 + j] = to_f<T>(pc[j]);
-    }
+// One Kogge-Stone level of the warp scans of (decay, value) pairs, with the shuffle's own
+// in-range predicate guarding the combine (predicated instructions instead of compare + select):
+// up:   lanes >= off combine with lane - off:  H = A H' + H, A = A A'   (forward states)
+// down: lanes < 32 - off combine with lane + off: Q = P Q' + Q, P = P P' (reverse adjoints)
+__device__ __forceinline__ void scan_up_level(float &A, float &H, int off) {
+    asm("{\n\t.reg .pred p;\n\t.reg .f32 ap, hp;\n\t"
+        "shfl.sync.up.b32 ap|p, %0, %2, 0, 0xffffffff;\n\t"
+        "shfl.sync.up.b32 hp, %1, %2, 0, 0xffffffff;\n\t"
+        "@p fma.rn.f32 %1, %0, hp, %1;\n\t"
+        "@p mul.rn.f32 %0, %0, ap;\n\t}"
+        : "+f"(A), "+f"(H) : "r"(off));
 }
-template <> __device__ __forceinline__ void bc_ld8<float>(const float *base, int lane, float (&v)[8]) {
-    ld8(base, lane, v);
+__device__ __forceinline__ void scan_down_level(float &P, float &Q, int off) {
+    asm("{\n\t.reg .pred p;\n\t.reg .f32 pr, qr;\n\t"
+        "shfl.sync.down.b32 pr|p, %0, %2, 31, 0xffffffff;\n\t"
+        "shfl.sync.down.b32 qr, %1, %2, 31, 0xffffffff;\n\t"
+        "@p fma.rn.f32 %1, %0, qr, %1;\n\t"
+        "@p mul.rn.f32 %0, %0, pr;\n\t}"
+        : "+f"(P), "+f"(Q) : "r"(off));
 }
-template <typename T> __device__ __forceinline__ void bc_st8(T *base, int lane, const float (&v)[8]) {
-    T a[4], c[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        a[j] = from_f<T>(v[j]);
-        c[j] = from_f<T>(v[4 + j]);
-    }
-    *reinterpret_cast<uint2 *>(base + lane * 4) = *reinterpret_cast<const uint2 *>(a);
-    *reinterpret_cast<uint2 *>(base + 128 + lane * 4) = *reinterpret_cast<const uint2 *>(c);
-}
+
 __device__ __forceinline__ void st8(float *base, int lane, const float (&v)[8]) {
     *reinterpret_cast<float4 *>(base + lane * 4) = make_float4(v[0], v[1], v[2], v[3]);
     *reinterpret_cast<float4 *>(base + 128 + lane * 4) = make_float4(v[4], v[5], v[6], v[7]);
@@ -197,7 +194,7 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
 #pragma unroll
                 for (int j = 0; j < 8; ++j) v[j] = 0.f;
             }
-            if constexpr (Smem::kPrefetch) bc_st8(&S.BC[q][n][0], l, v); else st8(&S.BC[q][n][0], l, v);
+            st8(&S.BC[q][n][0], l, v);
         }
         __syncthreads();
 
@@ -318,7 +315,7 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
                     A2p[s] = pack2(A2[s], A2[s]);
                     Anp[s] = pack2(An[s], An[s]);
                     float bv8[8];
-                    bc_ld8(&S.BC[0][n][0], lane, bv8);
+                    ld8(&S.BC[0][n][0], lane, bv8);
 #pragma unroll
                     for (int m = 0; m < 4; ++m) Bv[s][m] = pack2(bv8[2 * m], bv8[2 * m + 1]);
 #pragma unroll
@@ -337,7 +334,7 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
                 for (int s = 0; s < 2; ++s) {
                     const int n = n0 + s;
                     float cv8[8];
-                    bc_ld8(&S.BC[1][n][0], lane, cv8);
+                    ld8(&S.BC[1][n][0], lane, cv8);
                     const float2 e0 = unpack2(mul2(dog2[0], pack2(cv8[0], cv8[1])));
                     const float2 e1 = unpack2(mul2(dog2[1], pack2(cv8[2], cv8[3])));
                     const float2 e2v = unpack2(mul2(dog2[2], pack2(cv8[4], cv8[5])));
@@ -370,24 +367,10 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
                 }
 #pragma unroll
                 for (int off = 1; off < 32; off <<= 1) {
-                    float Ap[2], Hp[2], Pr[2], Qr[2];
 #pragma unroll
                     for (int s = 0; s < 2; ++s) {
-                        Ap[s] = __shfl_up_sync(FULL, Ad[s], off);
-                        Hp[s] = __shfl_up_sync(FULL, Hd[s], off);
-                        Pr[s] = __shfl_down_sync(FULL, Pd[s], off);
-                        Qr[s] = __shfl_down_sync(FULL, Qd[s], off);
-                    }
-#pragma unroll
-                    for (int s = 0; s < 2; ++s) {
-                        if (lane >= off) {
-                            Hd[s] = fmaf(Ad[s], Hp[s], Hd[s]);
-                            Ad[s] *= Ap[s];
-                        }
-                        if (lane + off < 32) {
-                            Qd[s] = fmaf(Pd[s], Qr[s], Qd[s]);
-                            Pd[s] *= Pr[s];
-                        }
+                        scan_up_level(Ad[s], Hd[s], off);
+                        scan_down_level(Pd[s], Qd[s], off);
                     }
                 }
                 float h_in[2], carry[2];
@@ -466,13 +449,17 @@ __global__ void __launch_bounds__(bwd::NT, 2) ss_bwd_kernel(const BwdParams p) {
                         }
                     }
                 }
+                {   // this channel's dA for both states: sum over the lanes.  The first level
+                    // hands each half-warp one state (lanes < 16 state n0, the others n0 + 1),
+                    // so the last four levels reduce one value instead of two.
+                    const float2 v0 = unpack2(dA2[0]), v1 = unpack2(dA2[1]);
+                    const float p0 = v0.x + v0.y, p1 = v1.x + v1.y;
+                    const bool upper = (lane & 16) != 0;
+                    float dAp = (upper ? p1 : p0) + __shfl_xor_sync(FULL, upper ? p0 : p1, 16);
 #pragma unroll
-                for (int s = 0; s < 2; ++s) {  // this channel's dA: sum over the lanes
-                    const float2 v = unpack2(dA2[s]);
-                    float dAp = v.x + v.y;
-#pragma unroll
-                    for (int off = 16; off > 0; off >>= 1) dAp += __shfl_xor_sync(FULL, dAp, off);
-                    if (lane == 0 && (s == 0 || has1)) S.DAACC[cg][w][n0 + s] += dAp;
+                    for (int off = 8; off > 0; off >>= 1) dAp += __shfl_xor_sync(FULL, dAp, off);
+                    if (lane == 0) S.DAACC[cg][w][n0] += dAp;
+                    if (lane == 16 && has1) S.DAACC[cg][w][n0 + 1] += dAp;
                 }
                 __syncthreads();  // the accumulator rows pass to the next warp
             }
