@@ -81,6 +81,12 @@ typedef struct {
      * P (dim, dstate, r) and Q (dim, r, dstate) when pq_per_dim; r = pq_rank <= 8, dstate <= 64. */
     const float *P;     const float *Q;
     int64_t pq_rank;    int32_t pq_per_dim; int32_t _pad_pq;
+    /* nullable: the state before the first step, fp32 contiguous (batch, dim, dstate), so a
+     * sequence can be scanned in pieces (the state at the end of one piece, x[:, :, -1, 1::2],
+     * starts the next; the decay halves of x then cover this call's steps only).  No
+     * counterpart in the reference's binding, which always starts from zero; forward only
+     * (ss_bwd assumes a zero initial state) and not with P/Q. */
+    const float *h0;
 } ss_fwd_args;
 
 typedef struct {

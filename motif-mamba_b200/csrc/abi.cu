@@ -214,6 +214,7 @@ int ss_fwd(const ss_fwd_args *a, void *stream) {
     p.A = a->A; p.A_ds = a->A_ds; p.A_ns = a->A_ns;
     p.D = a->D; p.D_s = a->D_s; p.delta_bias = a->delta_bias; p.delta_bias_s = a->delta_bias_s;
     p.x = a->x;
+    p.h0 = a->h0;
     p.ws_h = s.n_seg > 1 ? reinterpret_cast<float *>(a->workspace) : nullptr;
     p.ws_dts = s.n_seg > 1 ? reinterpret_cast<float *>(reinterpret_cast<char *>(a->workspace) + s.ws_h_bytes) : nullptr;
     bool aligned = al16(a->u) && al16(a->delta) && al16(a->B) && al16(a->C) && al16(a->out) &&
@@ -224,8 +225,11 @@ int ss_fwd(const ss_fwd_args *a, void *stream) {
         aligned = aligned && al16(a->z) && al16(a->out_z) && st16(a->z_bs, es) && st16(a->z_ds, es) &&
                   st16(a->out_z_bs, es) && st16(a->out_z_ds, es);
     p.aligned = aligned ? 1 : 0;
+    if (a->h0 && (reinterpret_cast<uintptr_t>(a->h0) & 3))
+        return fail(MSS_ERR_ALIGNMENT, "ss_fwd: h0 must be 4-byte aligned fp32");
     cudaError_t e;
     if (a->P) {
+        if (a->h0) return fail(MSS_ERR_UNSUPPORTED, "ss_fwd: an initial state is not supported with P/Q");
         p.P = a->P; p.Q = a->Q; p.pq_rank = (int)a->pq_rank; p.pq_per_dim = a->pq_per_dim ? 1 : 0;
         e = launch_ss_fwd_pq(p, a->itype, a->z != nullptr, static_cast<cudaStream_t>(stream));
     } else {

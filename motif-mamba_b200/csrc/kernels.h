@@ -24,6 +24,7 @@ struct FwdParams {
     float *ws_h, *ws_dts;  // segment carries (n_seg > 1)
     const float *P, *Q;    // motif coupling (nullptr: none)
     int pq_rank, pq_per_dim;
+    const float *h0;       // state before the first step (batch, dim, dstate), or nullptr (zero)
 };
 
 struct BwdParams {

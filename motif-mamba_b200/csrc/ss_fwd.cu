@@ -154,6 +154,11 @@ __global__ void __launch_bounds__(FwdCfg<NS, SPT>::NT, FwdCfg<NS, SPT>::MINB) ss
 #pragma unroll
         for (int m = 0; m < NP; ++m) h2[m] = pack2(H[2 * m], H[2 * m + 1]);
         cum = p.ws_dts[row * p.n_seg + s];
+    } else if (!CARRY && p.h0 != nullptr && valid) {  // the caller's state before the first step
+        const float *H = p.h0 + row * p.dstate + n0;
+#pragma unroll
+        for (int m = 0; m < NP; ++m)
+            h2[m] = pack2(n0 + 2 * m < p.dstate ? H[2 * m] : 0.f, n0 + 2 * m + 1 < p.dstate ? H[2 * m + 1] : 0.f);
     }
 
     const T *gu = reinterpret_cast<const T *>(p.u) + (int64_t)b * p.u_bs + (int64_t)c0 * p.u_ds;
@@ -308,13 +313,14 @@ __global__ void __launch_bounds__(FwdCfg<NS, SPT>::NT, FwdCfg<NS, SPT>::MINB) ss
 // from zero, and ws_dts[row][s] the summed dt over it; segment s's decay of state n is
 // exp(A_n * dts_s).  On exit, slot s + 1 holds the state at the start of segment s + 1 (the
 // composition (D, H) o (D', H') = (D D', D' H + H') over segments 0..s) and ws_dts slot s + 1
-// the summed dt before it.  G lanes (a power of two >= n_seg - 1, <= 32) per (row, state), one
+// the summed dt before it; a caller-given initial state h0 (if any) is composed in front of
+// segment 0.  G lanes (a power of two >= n_seg - 1, <= 32) per (row, state), one
 // lane per segment, a log2(G)-level shuffle scan: latency O(log n_seg) instead of a chain of
 // dependent loads per segment in the main pass.
 __global__ void __launch_bounds__(256) seg_carry_scan_kernel(float *__restrict__ ws_h, float *__restrict__ ws_dts,
                                                              const float *__restrict__ A, int64_t A_ds, int64_t A_ns,
                                                              int64_t rows, int dim, int dstate, int ns, int n_seg,
-                                                             int G) {
+                                                             int G, const float *__restrict__ h0) {
     const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int lane = threadIdx.x & (G - 1);          // segment
     const int64_t pair = tid / G;                     // (row, state)
@@ -342,6 +348,8 @@ __global__ void __launch_bounds__(256) seg_carry_scan_kernel(float *__restrict__
         }
     }
     if (live) {
+        // a caller-given state before segment 0 decays through segments 0..lane and adds on
+        if (h0 != nullptr && n < dstate) Hl = fmaf(Dl, h0[row * dstate + n], Hl);
         ws_h[(row * n_seg + lane + 1) * ns + n] = Hl;
         if (n == 0) ws_dts[row * n_seg + lane + 1] = Sl;
     }
@@ -374,7 +382,7 @@ static cudaError_t launch_spt(FwdParams p, bool has_z, cudaStream_t st) {
         while (G < p.n_seg - 1) G <<= 1;  // n_seg <= 33 (abi.cu caps it at 32)
         const int64_t threads = (int64_t)p.batch * p.dim * NS * G;
         seg_carry_scan_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
-            p.ws_h, p.ws_dts, p.A, p.A_ds, p.A_ns, (int64_t)p.batch * p.dim, p.dim, p.dstate, NS, p.n_seg, G);
+            p.ws_h, p.ws_dts, p.A, p.A_ds, p.A_ns, (int64_t)p.batch * p.dim, p.dim, p.dstate, NS, p.n_seg, G, p.h0);
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }

@@ -37,6 +37,7 @@ class SsFwdArgs(ctypes.Structure):
         ("workspace", vp), ("workspace_bytes", i64),
         ("P", vp), ("Q", vp),
         ("pq_rank", i64), ("pq_per_dim", i32), ("_pad_pq", i32),
+        ("h0", vp),
     ]
 
 

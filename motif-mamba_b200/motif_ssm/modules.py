@@ -22,6 +22,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .causal_conv1d import causal_conv1d_fn, causal_conv1d_update
+from . import selective_scan_cuda as _ssc
 from .selective_scan_interface import mamba_inner_fn, selective_scan_fn
 from .norm import add_rms_norm
 from .norm import supported as rms_fused_supported
@@ -462,25 +463,38 @@ class TPMambamotif(nn.Module):
                 m.P_eff, m.Q = P_eff.contiguous(), Q.contiguous()
         return m
 
-    def _all_reduce(self, t):
+    def _all_reduce(self, t, group=None):
         if self.world > 1:
-            torch.distributed.all_reduce(t, group=self.group)
+            torch.distributed.all_reduce(t, group=self.group if group is None else group)
         return t
 
+    # halo of the causal conv carried from one sequence chunk to the next: 8 steps (not
+    # d_conv - 1 = 3) so that the conv output of a chunk starts 16-byte aligned
+    HALO = 8
+
     @torch.no_grad()
-    def forward(self, hidden_states, inference_params=None):
+    def forward_chunk(self, hidden_states, carry, xproj_group=None):
+        """One sequence chunk of this shard's mixer.  ``carry`` holds what the next chunk needs
+        from this one (the pre-conv x tail and the fp32 scan state; empty dict for the first
+        chunk) and is updated.  Returns this rank's out_proj partial sum (not all-reduced);
+        the x_proj partial sums are all-reduced here (fp32, on ``xproj_group`` if given)."""
         batch, seqlen, _ = hidden_states.shape
         xz = (self.in_proj_w @ hidden_states.reshape(-1, self.d_model).t()).view(-1, batch, seqlen).transpose(0, 1)
         x, z = xz.chunk(2, dim=1)
-        x = causal_conv1d_fn(x, self.conv_w, self.conv_b, activation="silu")
+        tail = carry.get("x_tail")
+        xin = x if tail is None else torch.cat([tail, x], dim=-1)
+        carry["x_tail"] = x[..., -self.HALO:] if seqlen >= self.HALO else xin[..., -self.HALO:]
+        xc = causal_conv1d_fn(xin, self.conv_w, self.conv_b, activation="silu")
+        if tail is not None:
+            xc = xc[..., tail.shape[-1]:]
         # x_proj partial sums stay fp32 through the all-reduce and are rounded once, as the
         # unsharded GEMM rounds its fp32 accumulator once
-        xt = x.transpose(1, 2).reshape(-1, self.d_local)
+        xt = xc.transpose(1, 2).reshape(-1, self.d_local)
         if xt.dtype in (torch.bfloat16, torch.float16):
             x_dbl = torch.mm(xt, self.x_proj_w.t(), out_dtype=torch.float32)
         else:
             x_dbl = xt @ self.x_proj_w.t()
-        x_dbl = self._all_reduce(x_dbl.contiguous()).to(x.dtype)            # all-reduce #1
+        x_dbl = self._all_reduce(x_dbl.contiguous(), xproj_group).to(xc.dtype)   # all-reduce #1
         dt, B, C = torch.split(x_dbl, [self.dt_rank, self.d_state, self.d_state], dim=-1)
         dt = (self.dt_proj_w @ dt.t()).view(self.d_local, batch, seqlen).transpose(0, 1)
         B = B.reshape(batch, seqlen, -1).transpose(1, 2).contiguous()
@@ -488,10 +502,74 @@ class TPMambamotif(nn.Module):
         key = (self.A_log._version, self.A_log.data_ptr())
         if getattr(self, "_A_key", None) != key:  # A = -exp(A_log), once per change of A_log
             self._A, self._A_key = -torch.exp(self.A_log), key
-        y = selective_scan_fn(x, dt, self._A, B, C, self.D, z=z, delta_bias=self.dt_proj_b,
-                              delta_softplus=True, P=self.P_eff, Q=self.Q)
-        out = y.transpose(1, 2).reshape(-1, self.d_local) @ self.out_proj_w.t()
+        y, carry["h"] = _scan_chunk(xc, dt, self._A, B, C, self.D, z, self.dt_proj_b, carry.get("h"),
+                                    self.P_eff, self.Q)
+        return y.transpose(1, 2).reshape(-1, self.d_local) @ self.out_proj_w.t()
+
+    @torch.no_grad()
+    def forward(self, hidden_states, inference_params=None):
+        batch, seqlen, _ = hidden_states.shape
+        out = self.forward_chunk(hidden_states, {})
         return self._all_reduce(out.contiguous()).view(batch, seqlen, self.d_model)  # all-reduce #2
+
+
+def _scan_chunk(u, delta, A, B, C, D, z, delta_bias, h0, P=None, Q=None):
+    """The gated scan of one sequence chunk started from state ``h0`` (fp32 (b, d, n), None:
+    zero); returns (out_z, fp32 state after the chunk).  With P / Q (no initial-state support in
+    that kernel) the sequence must come as one chunk."""
+    if P is not None:
+        assert h0 is None, "the motif P/Q scan runs a sequence as one chunk"
+        y, last = selective_scan_fn(u, delta, A, B, C, D, z=z, delta_bias=delta_bias, delta_softplus=True,
+                                    return_last_state=True, P=P, Q=Q)
+        return y, last
+    out, x, out_z = _ssc.fwd(u, delta, A, B.unsqueeze(1), C.unsqueeze(1), D=D, z=z, delta_bias=delta_bias,
+                             delta_softplus=True, initial_state=h0)
+    return out_z, x[:, :, -1, 1::2].contiguous()
+
+
+@torch.no_grad()
+def tp_prefill(model, input_ids, n_chunks=4, num_last_tokens=1, groups=None):
+    """Prefill of a channel-sharded model (``shard_model_tp``) with the sequence split into
+    ``n_chunks`` chunks processed layer by layer, so that each chunk's out_proj all-reduce runs
+    on the NCCL stream while the next chunk's in_proj, conv, x_proj and scan run on the compute
+    stream (the scan carries its state across chunks, the conv an 8-step halo).  Layer l + 1's
+    chunk i waits only for layer l's chunk i.  ``groups`` = (x_proj group, out_proj group): two
+    communicators, so the small synchronous x_proj all-reduce of a chunk is not queued behind the
+    previous chunk's large out_proj all-reduce; by default two groups over all ranks are made
+    (and cached on the model).  Returns the logits of the last ``num_last_tokens`` tokens."""
+    import torch.distributed as dist
+    backbone = model.backbone
+    world = backbone.layers[0].mixer.world
+    if groups is None and world > 1:
+        groups = getattr(model, "_tp_groups", None)
+        if groups is None:
+            groups = (dist.new_group(), dist.new_group())
+            model._tp_groups = groups
+    g_x, g_out = groups if groups is not None else (None, None)
+    batch, seqlen = input_ids.shape
+    step = max(64, -(-seqlen // n_chunks + 63) // 64 * 64)  # chunk length: a multiple of 64 steps
+    bounds = [(t, min(seqlen, t + step)) for t in range(0, seqlen, step)]
+    emb = backbone.embedding(input_ids)
+    hid = [emb[:, t0:t1].contiguous() for t0, t1 in bounds]
+    res = [None] * len(bounds)
+    pend = [None] * len(bounds)
+    for layer in backbone.layers:
+        carry = {}
+        for i in range(len(bounds)):
+            if pend[i] is not None:
+                pend[i].wait()
+                pend[i] = None
+            normed, res[i] = add_norm(hid[i], res[i], layer.norm, layer.residual_in_fp32)
+            o = layer.mixer.forward_chunk(normed, carry, g_x)
+            if world > 1:
+                pend[i] = dist.all_reduce(o, group=g_out, async_op=True)  # all-reduce #2, overlapped
+            hid[i] = o.view(batch, bounds[i][1] - bounds[i][0], -1)
+    for w in pend:
+        if w is not None:
+            w.wait()
+    hidden = torch.cat(hid, dim=1)[:, -num_last_tokens:] if num_last_tokens > 0 else torch.cat(hid, dim=1)
+    residual = torch.cat(res, dim=1)[:, -hidden.shape[1]:]
+    return model.lm_head(add_norm(hidden, residual, backbone.norm_f)[0])
 
 
 def shard_model_tp(model, rank, world, group=None):

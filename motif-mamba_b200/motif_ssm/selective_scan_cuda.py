@@ -147,10 +147,20 @@ def n_chunks(seqlen):
 
 
 def fwd(u, delta, A, B, C, D=None, z=None, delta_bias=None, P=None, Q=None, gamma=None,
-        delta_softplus=False):
-    """Selective-scan forward.  Returns ``[out, x]`` plus ``out_z`` when ``z`` is given."""
+        delta_softplus=False, initial_state=None):
+    """Selective-scan forward.  Returns ``[out, x]`` plus ``out_z`` when ``z`` is given.
+
+    ``initial_state`` (an addition of this library; the reference always starts from zero):
+    fp32 contiguous (batch, dim, dstate), the state before the first step, so that a sequence
+    can be scanned in pieces -- ``x[:, :, -1, 1::2]`` of one piece starts the next.  Forward
+    only (``bwd`` assumes a zero initial state) and not with P / Q."""
     sizes = _check_common(u, delta, A, B, C, D, z, delta_bias, P, Q, gamma)
     batch, dim, seqlen, dstate, n_groups = sizes
+    if initial_state is not None:
+        _req(P is None, "initial_state is not supported with P / Q")
+        _req(initial_state.dtype == torch.float32 and initial_state.is_cuda and initial_state.is_contiguous(),
+             "initial_state must be a contiguous float32 CUDA tensor")
+        _check_shape(initial_state, batch, dim, dstate, name="initial_state")
     out = torch.empty_like(delta)
     x = torch.empty(batch, dim, n_chunks(seqlen), 2 * dstate, device=u.device, dtype=torch.float32)
     out_z = torch.empty_like(z) if z is not None else None
@@ -161,6 +171,7 @@ def fwd(u, delta, A, B, C, D=None, z=None, delta_bias=None, P=None, Q=None, gamm
     if z is not None:
         a.out_z, a.out_z_bs, a.out_z_ds = _ptr(out_z), out_z.stride(0), out_z.stride(1)
     a.x = _ptr(x)
+    a.h0 = _ptr(initial_state)
     ws_bytes = ctypes.c_int64(0)
     check(lib.ss_fwd_workspace_size(ctypes.byref(a), ctypes.byref(ws_bytes)))
     ws = None

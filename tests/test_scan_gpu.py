@@ -236,3 +236,31 @@ def test_scan_mixed_structure_in_one_cta(dstate):
     ref_out, ref_last, ref_grads = oracle(inp, dout, True)
     out, last, grads = run_kernel(inp, dout, True)
     compare(out, last, grads, ref_out, ref_last, ref_grads, torch.float32, "mixed A")
+
+
+@pytest.mark.parametrize("batch,dim,seqlen,dtype", [(2, 64, 1000, torch.float32), (1, 40, 4100, torch.float32),
+                                                    (2, 96, 2000, torch.bfloat16)])
+def test_initial_state_chains_sequence_pieces(batch, dim, seqlen, dtype):
+    """fwd(..., initial_state=h): scanning a sequence in pieces, each started from the previous
+    piece's final state x[:, :, -1, 1::2], gives the full scan's outputs and final state (the
+    second shape runs with the time split, whose carry scan composes h in front of segment 0)."""
+    from motif_ssm import selective_scan_cuda as ssc
+    inp, _ = make_scan_inputs(batch, dim, seqlen, 16, dtype, seed=31, device=DEV)
+    B, C = inp["B"].unsqueeze(1), inp["C"].unsqueeze(1)
+    kw = dict(D=inp["D"], delta_bias=inp["delta_bias"], delta_softplus=True)
+    out, x, out_z = ssc.fwd(inp["u"], inp["delta"], inp["A"], B, C, z=inp["z"], **kw)
+    cuts = [0, 300, 700, seqlen]
+    h, pieces, pieces_z = None, [], []
+    for t0, t1 in zip(cuts[:-1], cuts[1:]):
+        sl = lambda t: t[..., t0:t1]
+        o, xp, oz = ssc.fwd(sl(inp["u"]), sl(inp["delta"]), inp["A"], sl(B), sl(C), z=sl(inp["z"]), initial_state=h,
+                            **kw)
+        pieces.append(o)
+        pieces_z.append(oz)
+        h = xp[:, :, -1, 1::2].contiguous()
+    t = 1e-5 if dtype == torch.float32 else tol(dtype)
+    assert_close(torch.cat(pieces, -1), out, t, t, "out from pieces")
+    assert_close(torch.cat(pieces_z, -1), out_z, t, t, "out_z from pieces")
+    assert_close(h, x[:, :, -1, 1::2], 1e-5, 1e-5, "final state from pieces")
+    with pytest.raises(RuntimeError):
+        ssc.fwd(inp["u"], inp["delta"], inp["A"], B, C, z=inp["z"], initial_state=h[:, :1], **kw)

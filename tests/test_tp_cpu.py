@@ -34,13 +34,30 @@ def _patch_ops():
     def inner(*a, **k):
         return O.mamba_inner_ref(*a, **{kk: v for kk, v in k.items() if kk != "checkpoint_lvl"})
 
+    def scan_chunk(u, delta, A, B, C, D, z, delta_bias, h0, P=None, Q=None):
+        """The gated scan of a chunk from state h0: the oracle from zero plus h0's decayed
+        contribution (y_t += sum_n C_tn exp(A_n sum_{s<=t} dt_s) h0_n), gated afterwards."""
+        if P is not None:
+            assert h0 is None
+            return O.selective_scan_ref(u, delta, A, B, C, D, z=z, delta_bias=delta_bias, delta_softplus=True,
+                                        return_last_state=True, P=P, Q=Q)
+        out, last = O.selective_scan_ref(u, delta, A, B, C, D, z=None, delta_bias=delta_bias,
+                                         delta_softplus=True, return_last_state=True)
+        if h0 is not None:
+            dt = torch.nn.functional.softplus(delta.float() + delta_bias[:, None])
+            dec = torch.exp(A[None, :, None, :] * torch.cumsum(dt, dim=-1)[..., None])  # (b, d, l, n)
+            out = out + torch.einsum("bnl,bdln,bdn->bdl", C.float(), dec, h0)
+            last = last + dec[:, :, -1] * h0
+        return out * torch.nn.functional.silu(z.float()), last
+
     modules.causal_conv1d_fn = conv
     modules.selective_scan_fn = scan
     modules.mamba_inner_fn = inner
+    modules._scan_chunk = scan_chunk
     return modules
 
 
-def _worker(rank, world, port, q, pq_rank=0, pq_per_dim=False):
+def _worker(rank, world, port, q, pq_rank=0, pq_per_dim=False, n_chunks=0):
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path[:0] = [root, os.path.join(root, "motif-mamba_b200")]
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
@@ -58,11 +75,11 @@ def _worker(rank, world, port, q, pq_rank=0, pq_per_dim=False):
                     layer.mixer.pq_k.fill_(20.0)
                     layer.mixer.P.copy_(0.5 * torch.randn(layer.mixer.P.shape, generator=g))
                     layer.mixer.Q.copy_(0.5 * torch.randn(layer.mixer.Q.shape, generator=g))
-        ids = torch.randint(0, 40, (2, 24))
+        ids = torch.randint(0, 40, (2, 150 if n_chunks else 24))
         with torch.no_grad():
             ref = model(ids)
             modules.shard_model_tp(model, rank, world)
-            out = model(ids)
+            out = modules.tp_prefill(model, ids, n_chunks=n_chunks, num_last_tokens=0) if n_chunks else model(ids)
         q.put((rank, (out - ref).abs().max().item(), ref.abs().max().item()))
     finally:
         dist.destroy_process_group()
@@ -77,6 +94,23 @@ def test_tp2_gloo_matches_unsharded(pq_rank, pq_per_dim):
     q = ctx.Queue()
     port = _free_port()
     procs = [ctx.Process(target=_worker, args=(r, 2, port, q, pq_rank, pq_per_dim)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=240) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, err, scale in res:
+        assert err <= 1e-4 * max(1.0, scale), (rank, err, scale)
+
+
+def test_tp2_gloo_chunked_prefill_matches_unsharded():
+    """tp_prefill: the sequence in 3 chunks (64, 64, 22 steps) carried through the conv halo and
+    the scan state, out_proj all-reduces overlapped, two communicators."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, 0, False, 3)) for r in range(2)]
     for p in procs:
         p.start()
     res = [q.get(timeout=240) for _ in procs]
