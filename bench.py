@@ -262,7 +262,7 @@ def main():
     ap.add_argument("--global-batch", type=int, default=None,
                     help="prefill workload: override the global batch (e.g. 2 = one GPU's share at 8 GPUs)")
     ap.add_argument("--no-decode", action="store_true", help="prefill workload: skip the decode measurement")
-    ap.add_argument("--tp-chunks", type=int, default=4,
+    ap.add_argument("--tp-chunks", type=int, default=1,
                     help="tp workload: sequence chunks whose out_proj all-reduces overlap the next chunk's compute")
     ap.add_argument("--once", action="store_true", help="kernels workload: run each kernel twice (ncu capture)")
     ap.add_argument("--quick", action="store_true", help="refkernel workload: config 4 at seqlen 1024 only")
@@ -408,7 +408,7 @@ def tp_check(world, rank, dev, seqlen=1024, n_layer=2, n_chunks=2):
     (d_model 2560, d_inner 5120, n 16, dt_rank 160; 2 layers, vocab 512), bf16 random init
     with the same seed on every rank, 1 x 1024 random ids.  Rank 0 runs the unsharded model
     first; then every rank shards it and runs tp_prefill (the sequence in 2 chunks, x_proj
-    partial sums all-reduced in fp32, out_proj partial sums in bf16 over NCCL, overlapped).
+    partial sums all-reduced in fp32, out_proj partial sums in bf16 over NCCL, asynchronously).
     The logits of all tokens are compared on rank 0 with the bound used for sums throughout
     the tests, |a - e| <= 2e-2 max(1, max|e|) + 2e-2 |e| (logits are 2560-term dot products);
     the count of elements outside the plain elementwise bound 2e-2 + 2e-2 |e| is reported too."""
@@ -846,16 +846,21 @@ def run_tp(args):
     torch.manual_seed(0)
     model = MambaLMHeadModel(MambaConfig(d_model=2560, n_layer=n_layer, vocab_size=50277,
                                          ssm_cfg={"d_state": 16}), device=dev, dtype=torch.bfloat16)
-    shard_model_tp(model, rank, world, group)
+    if world > 1:
+        shard_model_tp(model, rank, world, group)
     torch.cuda.empty_cache()
     ids = torch.randint(0, 50277, (1, L), device=dev, generator=torch.Generator(device=dev).manual_seed(0))
     stream = torch.cuda.current_stream(dev)
 
     chunks = max(1, args.tp_chunks) if world > 1 else 1
 
-    def step():
+    def run():
+        if world == 1:  # one GPU: the unsharded model's own prefill path
+            with torch.no_grad():
+                return model(ids, num_last_tokens=1)
         return tp_prefill(model, ids, n_chunks=chunks, num_last_tokens=1)
 
+    step = run
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
@@ -878,8 +883,9 @@ def run_tp(args):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "64-layer stack d_model 2560 d_inner 5120 n 16 dt_rank 160, bf16 random init, "
                                    "prefill 1 x %d, last-token logits" % L, "parallelism": f"tp{world}",
-                       "seq_chunks": chunks, "overlap": "out_proj all-reduce of chunk i on a second NCCL "
-                                                        "communicator while chunk i+1 computes"},
+                       "seq_chunks": chunks,
+                       "overlap": "with seq_chunks > 1: out_proj all-reduce of chunk i issued asynchronously "
+                                  "while chunk i+1 computes"},
             "clocks": clk.summary(), "e2e": None, "cpu_baseline": None}), flush=True)
     if world > 1:
         dist.destroy_process_group()

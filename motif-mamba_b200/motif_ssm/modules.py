@@ -463,9 +463,9 @@ class TPMambamotif(nn.Module):
                 m.P_eff, m.Q = P_eff.contiguous(), Q.contiguous()
         return m
 
-    def _all_reduce(self, t, group=None):
+    def _all_reduce(self, t):
         if self.world > 1:
-            torch.distributed.all_reduce(t, group=self.group if group is None else group)
+            torch.distributed.all_reduce(t, group=self.group)
         return t
 
     # halo of the causal conv carried from one sequence chunk to the next: 8 steps (not
@@ -473,11 +473,11 @@ class TPMambamotif(nn.Module):
     HALO = 8
 
     @torch.no_grad()
-    def forward_chunk(self, hidden_states, carry, xproj_group=None):
+    def forward_chunk(self, hidden_states, carry):
         """One sequence chunk of this shard's mixer.  ``carry`` holds what the next chunk needs
         from this one (the pre-conv x tail and the fp32 scan state; empty dict for the first
         chunk) and is updated.  Returns this rank's out_proj partial sum (not all-reduced);
-        the x_proj partial sums are all-reduced here (fp32, on ``xproj_group`` if given)."""
+        the x_proj partial sums are all-reduced here (fp32)."""
         batch, seqlen, _ = hidden_states.shape
         xz = (self.in_proj_w @ hidden_states.reshape(-1, self.d_model).t()).view(-1, batch, seqlen).transpose(0, 1)
         x, z = xz.chunk(2, dim=1)
@@ -494,7 +494,7 @@ class TPMambamotif(nn.Module):
             x_dbl = torch.mm(xt, self.x_proj_w.t(), out_dtype=torch.float32)
         else:
             x_dbl = xt @ self.x_proj_w.t()
-        x_dbl = self._all_reduce(x_dbl.contiguous(), xproj_group).to(xc.dtype)   # all-reduce #1
+        x_dbl = self._all_reduce(x_dbl.contiguous()).to(xc.dtype)   # all-reduce #1
         dt, B, C = torch.split(x_dbl, [self.dt_rank, self.d_state, self.d_state], dim=-1)
         dt = (self.dt_proj_w @ dt.t()).view(self.d_local, batch, seqlen).transpose(0, 1)
         B = B.reshape(batch, seqlen, -1).transpose(1, 2).contiguous()
@@ -528,24 +528,18 @@ def _scan_chunk(u, delta, A, B, C, D, z, delta_bias, h0, P=None, Q=None):
 
 
 @torch.no_grad()
-def tp_prefill(model, input_ids, n_chunks=4, num_last_tokens=1, groups=None):
-    """Prefill of a channel-sharded model (``shard_model_tp``) with the sequence split into
-    ``n_chunks`` chunks processed layer by layer, so that each chunk's out_proj all-reduce runs
-    on the NCCL stream while the next chunk's in_proj, conv, x_proj and scan run on the compute
-    stream (the scan carries its state across chunks, the conv an 8-step halo).  Layer l + 1's
-    chunk i waits only for layer l's chunk i.  ``groups`` = (x_proj group, out_proj group): two
-    communicators, so the small synchronous x_proj all-reduce of a chunk is not queued behind the
-    previous chunk's large out_proj all-reduce; by default two groups over all ranks are made
-    (and cached on the model).  Returns the logits of the last ``num_last_tokens`` tokens."""
+def tp_prefill(model, input_ids, n_chunks=1, num_last_tokens=1):
+    """Prefill of a channel-sharded model (``shard_model_tp``), optionally with the sequence
+    split into ``n_chunks`` chunks processed layer by layer: each chunk's out_proj all-reduce is
+    issued asynchronously and waited for only when layer l + 1 reaches that chunk, so it can run
+    while the next chunk's in_proj, conv and x_proj GEMMs run (the scan carries its state across
+    chunks, the conv an 8-step halo).  All collectives go to the one communicator of the shards'
+    group, in the same order on every rank.  Returns the logits of the last ``num_last_tokens``
+    tokens (all of them for 0)."""
     import torch.distributed as dist
     backbone = model.backbone
-    world = backbone.layers[0].mixer.world
-    if groups is None and world > 1:
-        groups = getattr(model, "_tp_groups", None)
-        if groups is None:
-            groups = (dist.new_group(), dist.new_group())
-            model._tp_groups = groups
-    g_x, g_out = groups if groups is not None else (None, None)
+    mixer0 = backbone.layers[0].mixer
+    world, group = mixer0.world, mixer0.group
     batch, seqlen = input_ids.shape
     step = max(64, -(-seqlen // n_chunks + 63) // 64 * 64)  # chunk length: a multiple of 64 steps
     bounds = [(t, min(seqlen, t + step)) for t in range(0, seqlen, step)]
@@ -560,15 +554,17 @@ def tp_prefill(model, input_ids, n_chunks=4, num_last_tokens=1, groups=None):
                 pend[i].wait()
                 pend[i] = None
             normed, res[i] = add_norm(hid[i], res[i], layer.norm, layer.residual_in_fp32)
-            o = layer.mixer.forward_chunk(normed, carry, g_x)
+            o = layer.mixer.forward_chunk(normed, carry)
             if world > 1:
-                pend[i] = dist.all_reduce(o, group=g_out, async_op=True)  # all-reduce #2, overlapped
+                pend[i] = dist.all_reduce(o, group=group, async_op=True)  # all-reduce #2
             hid[i] = o.view(batch, bounds[i][1] - bounds[i][0], -1)
     for w in pend:
         if w is not None:
             w.wait()
-    hidden = torch.cat(hid, dim=1)[:, -num_last_tokens:] if num_last_tokens > 0 else torch.cat(hid, dim=1)
-    residual = torch.cat(res, dim=1)[:, -hidden.shape[1]:]
+    hidden = torch.cat(hid, dim=1)
+    residual = torch.cat(res, dim=1)
+    if num_last_tokens > 0:
+        hidden, residual = hidden[:, -num_last_tokens:], residual[:, -num_last_tokens:]
     return model.lm_head(add_norm(hidden, residual, backbone.norm_f)[0])
 
 

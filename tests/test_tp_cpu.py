@@ -106,7 +106,7 @@ def test_tp2_gloo_matches_unsharded(pq_rank, pq_per_dim):
 
 def test_tp2_gloo_chunked_prefill_matches_unsharded():
     """tp_prefill: the sequence in 3 chunks (64, 64, 22 steps) carried through the conv halo and
-    the scan state, out_proj all-reduces overlapped, two communicators."""
+    the scan state, out_proj all-reduces issued asynchronously."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
