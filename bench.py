@@ -466,6 +466,59 @@ def issue_ceiling(kernel, ms, clocks):
             "frac": achieved / peak}
 
 
+def host_link_probe(dev, stream, dist, nbytes=1 << 30, reps=3):
+    """Pinned host <-> device copy bandwidth of this rank, measured with all ranks copying at
+    the same time (as in the e2e step): one 1 GiB buffer each way, host-to-device alone,
+    device-to-host alone, then both at once on two streams; best of `reps`.  Also records the
+    CPU affinity of this process and the GPU's NUMA node, which decide whose memory controller
+    and PCIe root the pinned buffers cross.  Returns a dict (GB/s)."""
+    hbuf = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    hbuf2 = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    dbuf = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    dbuf2 = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    s2 = torch.cuda.Stream(dev)
+
+    def timed(fn):
+        best = float("inf")
+        for _ in range(reps):
+            if dist is not None:
+                dist.barrier()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            fn()
+            b.record(stream)
+            torch.cuda.synchronize()
+            best = min(best, a.elapsed_time(b))
+        return nbytes / (best * 1e-3) / 1e9
+
+    def both():
+        s2.wait_stream(stream)
+        dbuf.copy_(hbuf, non_blocking=True)
+        with torch.cuda.stream(s2):
+            hbuf2.copy_(dbuf2, non_blocking=True)
+        stream.wait_stream(s2)
+
+    rec = {"h2d_gbs": timed(lambda: dbuf.copy_(hbuf, non_blocking=True)),
+           "d2h_gbs": timed(lambda: hbuf2.copy_(dbuf2, non_blocking=True)),
+           "both_each_way_gbs": timed(both)}
+    try:
+        rec["cpu_affinity"] = len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        pass
+    try:  # NUMA node of this GPU's PCI device (sysfs, via the bus id NVML reports)
+        import pynvml  # nvidia_ml_py
+        pynvml.nvmlInit()
+        bus = pynvml.nvmlDeviceGetPciInfo(pynvml.nvmlDeviceGetHandleByIndex(dev.index)).busId
+        bus = (bus.decode() if isinstance(bus, bytes) else bus)[-12:].lower()
+        rec["gpu_pci"] = bus
+        rec["gpu_numa_node"] = int(open(f"/sys/bus/pci/devices/{bus}/numa_node").read().strip())
+    except Exception:
+        pass
+    del hbuf, hbuf2, dbuf, dbuf2
+    return rec
+
+
 def run_e2e(t, dout, dev, stream, world, selective_scan_fn, algo, steps, dist, n_sub=16):
     """selective_scan_fn (autograd) per step with host buffers: pinned host inputs ->
     device, forward, backward, all 8 gradients -> pinned host, timed with CUDA events
@@ -547,7 +600,13 @@ def run_e2e(t, dout, dev, stream, world, selective_scan_fn, algo, steps, dist, n
     if dist is not None:
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
     ms = tt.item() / steps
+    link = host_link_probe(dev, stream, dist)
+    links = [link]
+    if dist is not None:
+        links = [None] * world
+        dist.all_gather_object(links, link)
     return {"value": algo * world / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms, "steps": steps,
+            "host_links_per_rank": links,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "api": f"motif_ssm.selective_scan_fn forward + autograd backward on {n_sub} sub-batches, pinned host "
                    "buffers, host-to-device / compute / device-to-host pipelined on three streams"}
