@@ -50,8 +50,8 @@ FwdShape fwd_shape(const ss_fwd_args *a) {
     const int64_t capacity = (int64_t)kNumSMs * fwd_rows_per_sm((int)a->dstate, rows);
     const int64_t n_want = rows > 0 ? capacity / rows : 1;
     if (!a->P && rows > 0 && n_want >= 2 && a->seqlen >= 4 * 64) {
-        // at most 32 segments (the carry scan runs one lane per segment) of >= 64 steps
-        const int64_t n_max = std::min<int64_t>(std::min<int64_t>(n_want, 32), a->seqlen / 64);
+        // at most 128 segments (the carry scan composes up to 4 per lane of a warp) of >= 64 steps
+        const int64_t n_max = std::min<int64_t>(std::min<int64_t>(n_want, 128), a->seqlen / 64);
         int64_t seg = round_up((a->seqlen + n_max - 1) / n_max, 16);
         int64_t n = (a->seqlen + seg - 1) / seg;
         if (n > 1) {

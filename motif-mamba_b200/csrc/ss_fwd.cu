@@ -19,7 +19,7 @@
 // thread reads with broadcast 16-byte loads.  Outputs are written in place into the
 // staged u / z rows and leave through coalesced 16-byte stores.
 //
-// When batch * dim is too small to fill 148 SMs, the sequence is split into up to 32
+// When batch * dim is too small to fill 148 SMs, the sequence is split into up to 128
 // segments (whole 16-step tiles): a carry pass computes each segment's end state from zero
 // and its summed dt, a shuffle scan over segments (seg_carry_scan_kernel) composes them into
 // every segment's initial state (h_in = prod(decay) * h_in + H), and the main pass runs the
@@ -312,31 +312,42 @@ __global__ void __launch_bounds__(FwdCfg<NS, SPT>::NT, FwdCfg<NS, SPT>::MINB) ss
 // segment s < n_seg - 1, ws_h[row][s][n] holds H_s[n], the state at the end of segment s started
 // from zero, and ws_dts[row][s] the summed dt over it; segment s's decay of state n is
 // exp(A_n * dts_s).  On exit, slot s + 1 holds the state at the start of segment s + 1 (the
-// composition (D, H) o (D', H') = (D D', D' H + H') over segments 0..s) and ws_dts slot s + 1
-// the summed dt before it; a caller-given initial state h0 (if any) is composed in front of
-// segment 0.  G lanes (a power of two >= n_seg - 1, <= 32) per (row, state), one
-// lane per segment, a log2(G)-level shuffle scan: latency O(log n_seg) instead of a chain of
-// dependent loads per segment in the main pass.
+// composition (D, H) o (D', H') = (D D', D' H + H') over segments 0..s, applied to the
+// caller's initial state h0 when there is one) and ws_dts slot s + 1 the summed dt before it.
+// G lanes (a power of two, <= 32) per (row, state); lane l owns up to kSegPerLane consecutive
+// segments: it composes them, a log2(G)-level shuffle scan composes the lanes, and each lane
+// replays its segments from its exclusive prefix.  Latency O(kSegPerLane + log G) instead of a
+// chain of dependent loads per segment in the main pass.
+constexpr int kSegPerLane = 4;  // n_seg - 1 <= 32 * kSegPerLane carries
+
 __global__ void __launch_bounds__(256) seg_carry_scan_kernel(float *__restrict__ ws_h, float *__restrict__ ws_dts,
                                                              const float *__restrict__ A, int64_t A_ds, int64_t A_ns,
                                                              int64_t rows, int dim, int dstate, int ns, int n_seg,
-                                                             int G, const float *__restrict__ h0) {
+                                                             int G, int spl, const float *__restrict__ h0) {
     const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const int lane = threadIdx.x & (G - 1);          // segment
+    const int lane = threadIdx.x & (G - 1);
     const int64_t pair = tid / G;                     // (row, state)
     const bool in = pair < rows * ns;
     const int64_t row = in ? pair / ns : 0;
     const int n = in ? (int)(pair - row * ns) : 0;
     const int d = (int)(row % dim);
-    const bool live = in && lane < n_seg - 1;         // segments that have a carry
+    const int ncarry = n_seg - 1;                     // segments that have a carry
+    const int s0 = lane * spl;                        // this lane's first segment
     const float a2 = (in && n < dstate) ? A[(int64_t)d * A_ds + (int64_t)n * A_ns] * kLog2e : 0.f;
-    float H = 0.f, dts = 0.f;
-    if (live) {
-        H = ws_h[(row * n_seg + lane) * ns + n];
-        dts = ws_dts[row * n_seg + lane];
+    float Hk[kSegPerLane], Dk[kSegPerLane], Sk[kSegPerLane];
+    float Dl = 1.f, Hl = 0.f, Sl = 0.f;               // composite of this lane's segments
+#pragma unroll
+    for (int k = 0; k < kSegPerLane; ++k) {
+        const int sg = s0 + k;
+        const bool live = in && k < spl && sg < ncarry;
+        Hk[k] = live ? ws_h[(row * n_seg + sg) * ns + n] : 0.f;
+        Sk[k] = live ? ws_dts[row * n_seg + sg] : 0.f;
+        Dk[k] = live ? ex2(a2 * Sk[k]) : 1.f;
+        Hl = fmaf(Dk[k], Hl, Hk[k]);
+        Dl *= Dk[k];
+        Sl += Sk[k];
     }
-    // inclusive scan over the group's lanes: (Dl, Hl) composite of segments 0..lane; Sl = summed dt
-    float Dl = live ? ex2(a2 * dts) : 1.f, Hl = H, Sl = dts;
+    // inclusive scan over the group's lanes, then the exclusive prefix from the lane below
     for (int off = 1; off < G; off <<= 1) {
         const float Dp = __shfl_up_sync(0xffffffffu, Dl, off, G);
         const float Hp = __shfl_up_sync(0xffffffffu, Hl, off, G);
@@ -347,11 +358,22 @@ __global__ void __launch_bounds__(256) seg_carry_scan_kernel(float *__restrict__
             Sl += Sp;
         }
     }
-    if (live) {
-        // a caller-given state before segment 0 decays through segments 0..lane and adds on
-        if (h0 != nullptr && n < dstate) Hl = fmaf(Dl, h0[row * dstate + n], Hl);
-        ws_h[(row * n_seg + lane + 1) * ns + n] = Hl;
-        if (n == 0) ws_dts[row * n_seg + lane + 1] = Sl;
+    float De = __shfl_up_sync(0xffffffffu, Dl, 1, G), He = __shfl_up_sync(0xffffffffu, Hl, 1, G);
+    float Se = __shfl_up_sync(0xffffffffu, Sl, 1, G);
+    if (lane == 0) De = 1.f, He = 0.f, Se = 0.f;
+    // state before this lane's first segment, with the caller's initial state decayed through
+    // every earlier segment
+    float h = (h0 != nullptr && in && n < dstate) ? fmaf(De, h0[row * dstate + n], He) : He;
+    float cum = Se;
+#pragma unroll
+    for (int k = 0; k < kSegPerLane; ++k) {
+        const int sg = s0 + k;
+        if (in && k < spl && sg < ncarry) {
+            h = fmaf(Dk[k], h, Hk[k]);
+            cum += Sk[k];
+            ws_h[(row * n_seg + sg + 1) * ns + n] = h;
+            if (n == 0) ws_dts[row * n_seg + sg + 1] = cum;
+        }
     }
 }
 
@@ -378,11 +400,14 @@ static cudaError_t launch_spt(FwdParams p, bool has_z, cudaStream_t st) {
         dim3 gc(grid.x, p.n_seg - 1, grid.z);
         e = launch_one<T, NS, SPT, false, true>(p, gc, st);
         if (e != cudaSuccess) return e;
+        const int ncarry = p.n_seg - 1;
+        const int spl = (ncarry + 31) / 32;  // abi.cu caps n_seg at 32 * kSegPerLane + 1
         int G = 2;
-        while (G < p.n_seg - 1) G <<= 1;  // n_seg <= 33 (abi.cu caps it at 32)
+        while (G * spl < ncarry) G <<= 1;
         const int64_t threads = (int64_t)p.batch * p.dim * NS * G;
         seg_carry_scan_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
-            p.ws_h, p.ws_dts, p.A, p.A_ds, p.A_ns, (int64_t)p.batch * p.dim, p.dim, p.dstate, NS, p.n_seg, G, p.h0);
+            p.ws_h, p.ws_dts, p.A, p.A_ds, p.A_ns, (int64_t)p.batch * p.dim, p.dim, p.dstate, NS, p.n_seg, G, spl,
+            p.h0);
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
