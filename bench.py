@@ -202,13 +202,13 @@ def _cpu_record(dim_s, dt, threads, n_samples):
                        f"{dim_s} channels) / its time, i.e. the same per-element rate applied to the full workload")
 
 
-def cpu_baseline_sample(n_timed=2):
+def cpu_baseline_sample(n_timed=3):
     """The repo arm's cpu_baseline: the same fixed sample and thread count as the reference arm."""
     threads = cpu_threads()
     torch.set_num_threads(threads)
     _cpu_scan_seconds(CPU_SAMPLE_DIM)  # warm-up (first-call costs)
     ts = [_cpu_scan_seconds(CPU_SAMPLE_DIM) for _ in range(n_timed)]
-    dt = statistics.median(ts)
+    dt = min(ts)
     return _cpu_record(CPU_SAMPLE_DIM, dt, threads, n_timed), dt
 
 
@@ -229,7 +229,7 @@ def run_reference(args, budget_s=200.0):
         times.append(_cpu_scan_seconds(CPU_SAMPLE_DIM))
         if time.perf_counter() - t_start > budget_s:
             break
-    dt = statistics.median(times)
+    dt = min(times)
     cb = _cpu_record(CPU_SAMPLE_DIM, dt, threads, len(times))
     v = cb["value"]
     fwd_b, bwd_b = algo_bytes(**CFG)
