@@ -196,8 +196,9 @@ def _cpu_record(dim_s, dt, threads, n_samples):
     return dict(value=(f + b) / dt / 1e9, unit="GB/s", cores=threads, kind="port",
                 m_elements_per_s=dim_s * l / dt / 1e6,
                 sample=f"selective_scan_ref fwd + autograd bwd (oracle restatement), fixed sample batch 1 x {dim_s} "
-                       f"channels x seqlen {l}, n {n}, seed 0, bf16 inputs, fp32 math, {threads} threads: median "
-                       f"{dt:.2f} s over {n_samples} timed samples after 1 warm-up ({dim_s * l / dt / 1e6:.4f} M "
+                       f"channels x seqlen {l}, n {n}, seed 0, bf16 inputs, fp32 math, {threads} threads: fastest "
+                       f"{dt:.2f} s of {n_samples} timed samples after 1 warm-up (host cores are shared with other "
+                       f"jobs; the fastest sample is the least disturbed) ({dim_s * l / dt / 1e6:.4f} M "
                        f"elements/s); GB/s = the sample's algorithmic bytes (the metric's formula at batch 1 x "
                        f"{dim_s} channels) / its time, i.e. the same per-element rate applied to the full workload")
 
