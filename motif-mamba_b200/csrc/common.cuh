@@ -14,8 +14,8 @@
 namespace mss {
 
 constexpr int kChunkLen = 256;     // timesteps per x chunk (ss_chunk_len)
-constexpr int kMaxDstate = 64;     // largest dstate the forward accepts
-constexpr int kMaxDstateBwd = 64;  // largest dstate the backward accepts (blocks of 16)
+constexpr int kMaxDstate = 256;    // largest dstate the forward accepts (the reference's limit)
+constexpr int kMaxDstateBwd = 256; // largest dstate the backward accepts (blocks of 16)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kNumSMs = 148;      // B200 SMs (launch shapes are sized for one wave of them)
 

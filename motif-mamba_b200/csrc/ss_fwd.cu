@@ -36,7 +36,9 @@ int fwd_state_pad(int dstate) {
     if (dstate <= 8) return 8;
     if (dstate <= 16) return 16;
     if (dstate <= 32) return 32;
-    return 64;
+    if (dstate <= 64) return 64;
+    if (dstate <= 128) return 128;
+    return 256;
 }
 
 template <int NS, int SPT> struct FwdCfg {
@@ -58,15 +60,17 @@ template <int NS, int SPT> struct FwdCfg {
     static constexpr int MINB = NS <= 16 ? 8 : (SPT == 16 ? 4 : (LPC == 1 ? 2 : 3));
 };
 
-// Resident rows per SM of the variant fwd_spt picks (sizes the time split).
+// Resident rows per SM of the variant fwd_spt picks (sizes the time split).  dstate 128 / 256
+// rows run 8 / 16 lanes of 16 states, 3 CTAs per SM (shared memory: the fp32 B / C tile).
 static int rows_per_sm(int ns, int spt) {
     if (ns <= 16) return 768;
-    const int lpc = ns / spt, minb = spt == 16 ? 4 : (lpc == 1 ? 2 : 3);
+    const int lpc = ns / spt, minb = ns > 64 ? 3 : (spt == 16 ? 4 : (lpc == 1 ? 2 : 3));
     return minb * 128 / lpc;
 }
 
 int fwd_spt(int ns, int64_t rows) {
     if (ns <= 16) return ns;
+    if (ns > 64) return 16;         // 8 or 16 lanes of 16 states per row
     const int whole = ns;           // one thread per row
     const int half = ns / 2;        // two threads per row
     return rows >= (int64_t)kNumSMs * rows_per_sm(ns, whole) ? whole : half;
@@ -419,6 +423,8 @@ template <typename T, int NS>
 static cudaError_t launch_ns(const FwdParams &p, bool has_z, cudaStream_t st) {
     if constexpr (NS <= 16) {
         return launch_spt<T, NS, NS>(p, has_z, st);
+    } else if constexpr (NS > 64) {
+        return launch_spt<T, NS, 16>(p, has_z, st);
     } else {
         if (fwd_spt(NS, (int64_t)p.batch * p.dim) == NS) return launch_spt<T, NS, NS>(p, has_z, st);
         return launch_spt<T, NS, NS / 2>(p, has_z, st);
@@ -433,7 +439,9 @@ static cudaError_t launch_t(const FwdParams &p, bool has_z, cudaStream_t st) {
         case 8: return launch_ns<T, 8>(p, has_z, st);
         case 16: return launch_ns<T, 16>(p, has_z, st);
         case 32: return launch_ns<T, 32>(p, has_z, st);
-        default: return launch_ns<T, 64>(p, has_z, st);
+        case 64: return launch_ns<T, 64>(p, has_z, st);
+        case 128: return launch_ns<T, 128>(p, has_z, st);
+        default: return launch_ns<T, 256>(p, has_z, st);
     }
 }
 

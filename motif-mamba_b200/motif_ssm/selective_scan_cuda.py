@@ -10,7 +10,8 @@ Differences from the reference, all raising instead of silently diverging:
 * ``P`` / ``Q`` (the motif low-rank coupling, ``:342-369``) must be contiguous fp32 with
   ``dstate <= 64`` (the reference allows 256); ``gamma`` is checked and, as in the
   reference's dense P/Q kernels, not used;
-* ``dstate`` above ``MAX_DSTATE`` (64) raises (the reference allows 256);
+* ``dstate`` up to ``MAX_DSTATE`` (256, the reference's limit; above 64 a row's states are
+  spread over 8 or 16 lanes in the forward and the backward runs blocks of 16 states);
 * ``x`` holds one (decay, state) pair per ``CHUNK_LEN`` = 256 steps instead of 2048;
   ``x[:, :, -1, 1::2]`` is still the final state and ``bwd`` expects this ``x``.
 """

@@ -87,6 +87,10 @@ CASES = [
     # a wave of rows or more: dstate 32 / 64 rows in one thread each
     (38, 1000, 20, 32, torch.bfloat16, 0, True, True, True, True),
     (40, 1000, 17, 64, torch.float32, 0, False, True, True, True),
+    # dstate above 64 (up to the reference's 256): 8 / 16 lanes of 16 states per row, 16-state blocks
+    (1, 16, 300, 100, torch.float32, 0, True, True, True, True),
+    (2, 12, 270, 128, torch.bfloat16, 0, True, True, True, True),
+    (1, 8, 600, 256, torch.float32, 2, True, True, True, True),
 ]
 
 
