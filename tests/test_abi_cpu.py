@@ -91,7 +91,7 @@ def test_fwd_workspace_policy():
 
 def test_bwd_rejects_large_dstate_and_mismatched_grads():
     a = _lib.SsBwdArgs()
-    a.batch, a.dim, a.seqlen, a.dstate, a.n_groups, a.itype = 1, 8, 64, 128, 1, _lib.MSS_F32
+    a.batch, a.dim, a.seqlen, a.dstate, a.n_groups, a.itype = 1, 8, 64, 300, 1, _lib.MSS_F32
     assert _lib.lib.ss_bwd(ctypes.byref(a), None) == _lib.MSS_ERR_UNSUPPORTED
     a.dstate = 16
     a.D = 1234  # D given without dD

@@ -51,8 +51,9 @@ class _Recorder:
 
 
 def _scan_fwd(u, delta, A, B, C, D=None, z=None, delta_bias=None, P=None, Q=None, gamma=None,
-              delta_softplus=False):
+              delta_softplus=False, initial_state=None):
     from motif_ssm import selective_scan_cuda as ssc
+    assert initial_state is None  # the reference never passes this library's extra argument
     with torch.no_grad():
         out_z_or_out, last = O.selective_scan_ref(u, delta, A, B, C, D, z=z, delta_bias=delta_bias,
                                                   delta_softplus=delta_softplus, return_last_state=True, P=P, Q=Q)
