@@ -50,7 +50,7 @@ FwdShape fwd_shape(const ss_fwd_args *a) {
     const int64_t capacity = (int64_t)kNumSMs * fwd_rows_per_sm((int)a->dstate, rows);
     const int64_t n_want = rows > 0 ? capacity / rows : 1;
     if (!a->P && rows > 0 && n_want >= 2 && a->seqlen >= 4 * 64) {
-        // at most 128 segments (the carry scan composes up to 4 per lane of a warp) of >= 64 steps
+        // at most 128 segments of >= 64 steps
         const int64_t n_max = std::min<int64_t>(std::min<int64_t>(n_want, 128), a->seqlen / 64);
         int64_t seg = round_up((a->seqlen + n_max - 1) / n_max, 16);
         int64_t n = (a->seqlen + seg - 1) / seg;
@@ -59,7 +59,7 @@ FwdShape fwd_shape(const ss_fwd_args *a) {
             s.seg_len = (int)seg;
             const int ns = fwd_state_pad((int)a->dstate);
             s.ws_h_bytes = round_up(rows * n * ns * 4, 256);
-            s.ws_dts_bytes = round_up(rows * n * 4, 256);
+            s.ws_dts_bytes = round_up(2 * rows * n * 4, 256);  // raw and composed dt sums
         }
     }
     return s;

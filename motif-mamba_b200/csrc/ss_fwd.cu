@@ -21,7 +21,7 @@
 //
 // When batch * dim is too small to fill 148 SMs, the sequence is split into up to 128
 // segments (whole 16-step tiles): a carry pass computes each segment's end state from zero
-// and its summed dt, a shuffle scan over segments (seg_carry_scan_kernel) composes them into
+// and its summed dt, a pass over segments (seg_carry_scan_kernel) composes them into
 // every segment's initial state (h_in = prod(decay) * h_in + H), and the main pass runs the
 // full scan of each segment from its initial state.
 #include <type_traits>
@@ -153,11 +153,11 @@ __global__ void __launch_bounds__(FwdCfg<NS, SPT>::NT, FwdCfg<NS, SPT>::MINB) ss
     const int64_t row = (int64_t)b * p.dim + d;
     if (!CARRY && s > 0 && valid) {
         // initial state of this segment and the summed dt before it, left in the workspace by
-        // seg_carry_scan_kernel (the carries of the earlier segments composed in log depth)
+        // seg_carry_scan_kernel (the carries of the earlier segments composed in order)
         const float *H = p.ws_h + (row * p.n_seg + s) * NS + n0;
 #pragma unroll
         for (int m = 0; m < NP; ++m) h2[m] = pack2(H[2 * m], H[2 * m + 1]);
-        cum = p.ws_dts[row * p.n_seg + s];
+        cum = p.ws_dts[(int64_t)p.batch * p.dim * p.n_seg + row * p.n_seg + s];
     } else if (!CARRY && p.h0 != nullptr && valid) {  // the caller's state before the first step
         const float *H = p.h0 + row * p.dstate + n0;
 #pragma unroll
@@ -315,68 +315,61 @@ __global__ void __launch_bounds__(FwdCfg<NS, SPT>::NT, FwdCfg<NS, SPT>::MINB) ss
 // Turns the per-segment carries into per-segment initial states.  On entry, for every row and
 // segment s < n_seg - 1, ws_h[row][s][n] holds H_s[n], the state at the end of segment s started
 // from zero, and ws_dts[row][s] the summed dt over it; segment s's decay of state n is
-// exp(A_n * dts_s).  On exit, slot s + 1 holds the state at the start of segment s + 1 (the
-// composition (D, H) o (D', H') = (D D', D' H + H') over segments 0..s, applied to the
-// caller's initial state h0 when there is one) and ws_dts slot s + 1 the summed dt before it.
-// G lanes (a power of two, <= 32) per (row, state); lane l owns up to kSegPerLane consecutive
-// segments: it composes them, a log2(G)-level shuffle scan composes the lanes, and each lane
-// replays its segments from its exclusive prefix.  Latency O(kSegPerLane + log G) instead of a
-// chain of dependent loads per segment in the main pass.
-constexpr int kSegPerLane = 4;  // n_seg - 1 <= 32 * kSegPerLane carries
-
+// exp(A_n * dts_s).  On exit, slot s + 1 of ws_h holds the state at the start of segment s + 1
+// (the composition h = exp(A_n dts_s) h + H_s over segments 0..s, applied to the caller's
+// initial state h0 when there is one), and slot s + 1 of the second half of ws_dts (offset
+// rows * n_seg) the summed dt before segment s + 1; the raw sums stay untouched, because every
+// thread of a row reads them while its state-0 thread writes the composed sums.
+// One thread per (row, state), consecutive threads on consecutive states (coalesced rows of
+// ws_h), walking the segments in order: the dependency between segments is one FMA.  The
+// carries of kSegBatch segments are loaded together and the next batch's loads are issued
+// before the current batch is composed, so the kernel costs about one memory latency per
+// batch (kSegBatch = 4 when there are at most 4 carries: fewer registers, more resident
+// threads).  A thread reads slot s + 1 of ws_h (segment s + 1's carry) before it overwrites
+// that slot with segment s + 1's initial state.
+template <int kSegBatch>
 __global__ void __launch_bounds__(256) seg_carry_scan_kernel(float *__restrict__ ws_h, float *__restrict__ ws_dts,
                                                              const float *__restrict__ A, int64_t A_ds, int64_t A_ns,
                                                              int64_t rows, int dim, int dstate, int ns, int n_seg,
-                                                             int G, int spl, const float *__restrict__ h0) {
+                                                             const float *__restrict__ h0) {
     const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const int lane = threadIdx.x & (G - 1);
-    const int64_t pair = tid / G;                     // (row, state)
-    const bool in = pair < rows * ns;
-    const int64_t row = in ? pair / ns : 0;
-    const int n = in ? (int)(pair - row * ns) : 0;
+    if (tid >= rows * ns) return;
+    const int64_t row = tid / ns;
+    const int n = (int)(tid - row * ns);
     const int d = (int)(row % dim);
-    const int ncarry = n_seg - 1;                     // segments that have a carry
-    const int s0 = lane * spl;                        // this lane's first segment
-    const float a2 = (in && n < dstate) ? A[(int64_t)d * A_ds + (int64_t)n * A_ns] * kLog2e : 0.f;
-    float Hk[kSegPerLane], Dk[kSegPerLane], Sk[kSegPerLane];
-    float Dl = 1.f, Hl = 0.f, Sl = 0.f;               // composite of this lane's segments
+    const float a2 = n < dstate ? A[(int64_t)d * A_ds + (int64_t)n * A_ns] * kLog2e : 0.f;
+    float h = (h0 != nullptr && n < dstate) ? h0[row * dstate + n] : 0.f;
+    float cum = 0.f;
+    const int ncarry = n_seg - 1;
+    float *H = ws_h + row * n_seg * ns + n;           // slot s at H[s * ns]
+    const float *S = ws_dts + row * n_seg;            // raw sums
+    float *Sc = ws_dts + rows * n_seg + row * n_seg;  // composed sums
+    float hk[kSegBatch], sk[kSegBatch], hn[kSegBatch] = {}, sn[kSegBatch] = {};
+    auto load = [&](int s0, float (&hv)[kSegBatch], float (&sv)[kSegBatch]) {
 #pragma unroll
-    for (int k = 0; k < kSegPerLane; ++k) {
-        const int sg = s0 + k;
-        const bool live = in && k < spl && sg < ncarry;
-        Hk[k] = live ? ws_h[(row * n_seg + sg) * ns + n] : 0.f;
-        Sk[k] = live ? ws_dts[row * n_seg + sg] : 0.f;
-        Dk[k] = live ? ex2(a2 * Sk[k]) : 1.f;
-        Hl = fmaf(Dk[k], Hl, Hk[k]);
-        Dl *= Dk[k];
-        Sl += Sk[k];
-    }
-    // inclusive scan over the group's lanes, then the exclusive prefix from the lane below
-    for (int off = 1; off < G; off <<= 1) {
-        const float Dp = __shfl_up_sync(0xffffffffu, Dl, off, G);
-        const float Hp = __shfl_up_sync(0xffffffffu, Hl, off, G);
-        const float Sp = __shfl_up_sync(0xffffffffu, Sl, off, G);
-        if (lane >= off) {
-            Hl = fmaf(Dl, Hp, Hl);
-            Dl *= Dp;
-            Sl += Sp;
+        for (int k = 0; k < kSegBatch; ++k) {
+            const bool live = s0 + k < ncarry;
+            hv[k] = live ? H[(int64_t)(s0 + k) * ns] : 0.f;
+            sv[k] = live ? S[s0 + k] : 0.f;
         }
-    }
-    float De = __shfl_up_sync(0xffffffffu, Dl, 1, G), He = __shfl_up_sync(0xffffffffu, Hl, 1, G);
-    float Se = __shfl_up_sync(0xffffffffu, Sl, 1, G);
-    if (lane == 0) De = 1.f, He = 0.f, Se = 0.f;
-    // state before this lane's first segment, with the caller's initial state decayed through
-    // every earlier segment
-    float h = (h0 != nullptr && in && n < dstate) ? fmaf(De, h0[row * dstate + n], He) : He;
-    float cum = Se;
+    };
+    load(0, hk, sk);
+    for (int s0 = 0; s0 < ncarry; s0 += kSegBatch) {
+        // the next batch's carries (slot s0 + kSegBatch included) before any store of this batch
+        if (s0 + kSegBatch < ncarry) load(s0 + kSegBatch, hn, sn);
 #pragma unroll
-    for (int k = 0; k < kSegPerLane; ++k) {
-        const int sg = s0 + k;
-        if (in && k < spl && sg < ncarry) {
-            h = fmaf(Dk[k], h, Hk[k]);
-            cum += Sk[k];
-            ws_h[(row * n_seg + sg + 1) * ns + n] = h;
-            if (n == 0) ws_dts[row * n_seg + sg + 1] = cum;
+        for (int k = 0; k < kSegBatch; ++k) {
+            if (s0 + k < ncarry) {
+                h = fmaf(ex2(a2 * sk[k]), h, hk[k]);
+                cum += sk[k];
+                H[(int64_t)(s0 + k + 1) * ns] = h;
+                if (n == 0) Sc[s0 + k + 1] = cum;
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < kSegBatch; ++k) {
+            hk[k] = hn[k];
+            sk[k] = sn[k];
         }
     }
 }
@@ -404,14 +397,14 @@ static cudaError_t launch_spt(FwdParams p, bool has_z, cudaStream_t st) {
         dim3 gc(grid.x, p.n_seg - 1, grid.z);
         e = launch_one<T, NS, SPT, false, true>(p, gc, st);
         if (e != cudaSuccess) return e;
-        const int ncarry = p.n_seg - 1;
-        const int spl = (ncarry + 31) / 32;  // abi.cu caps n_seg at 32 * kSegPerLane + 1
-        int G = 2;
-        while (G * spl < ncarry) G <<= 1;
-        const int64_t threads = (int64_t)p.batch * p.dim * NS * G;
-        seg_carry_scan_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
-            p.ws_h, p.ws_dts, p.A, p.A_ds, p.A_ns, (int64_t)p.batch * p.dim, p.dim, p.dstate, NS, p.n_seg, G, spl,
-            p.h0);
+        const int64_t threads = (int64_t)p.batch * p.dim * NS;
+        const unsigned nb = (unsigned)((threads + 255) / 256);
+        if (p.n_seg - 1 <= 4)
+            seg_carry_scan_kernel<4><<<nb, 256, 0, st>>>(p.ws_h, p.ws_dts, p.A, p.A_ds, p.A_ns,
+                                                        (int64_t)p.batch * p.dim, p.dim, p.dstate, NS, p.n_seg, p.h0);
+        else
+            seg_carry_scan_kernel<16><<<nb, 256, 0, st>>>(p.ws_h, p.ws_dts, p.A, p.A_ds, p.A_ns,
+                                                         (int64_t)p.batch * p.dim, p.dim, p.dstate, NS, p.n_seg, p.h0);
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }

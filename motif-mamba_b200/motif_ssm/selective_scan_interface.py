@@ -180,6 +180,11 @@ def rms_norm_forward(x, weight, bias, eps=1e-6, is_rms_norm=True):
                            residual_dtype=None, is_rms_norm=is_rms_norm)[0]
 
 
+def _bcast(w, batch):
+    """A weight matrix as a (batch, m, k) operand of a batched product (batch stride 0, no copy)."""
+    return w.unsqueeze(0).expand(batch, -1, -1)
+
+
 class MambaInnerFn(torch.autograd.Function):
 
     @staticmethod
@@ -204,10 +209,11 @@ class MambaInnerFn(torch.autograd.Function):
         x, z = xz.chunk(2, dim=1)
         conv1d_bias = conv1d_bias.contiguous() if conv1d_bias is not None else None
         conv_out = causal_conv1d_fwd_function(x, w_conv, conv1d_bias, None, None, None, True)
-        # (b, d, l) -> (b*l, d) rows for x_proj; delta comes back as a (b, d, l) view of a
-        # (d, b*l) product, so l stays unit-stride without a transpose copy.
-        x_dbl = F.linear(conv_out.transpose(1, 2).reshape(-1, conv_out.shape[1]), x_proj_weight)
-        delta = (delta_proj_weight @ x_dbl[:, :rank].t()).view(-1, xz.shape[0], L).transpose(0, 1)
+        # x_proj as a batched product in the scan's (b, d, l) layout: x_dbl is (b, dt_rank + 2n, l),
+        # so delta (dt_proj), B and C come out with l unit-stride and need no transpose copies
+        # (B / C are strided views of x_dbl's rows).
+        x_dbl = torch.bmm(_bcast(x_proj_weight, conv_out.shape[0]), conv_out)
+        delta = torch.bmm(_bcast(delta_proj_weight, conv_out.shape[0]), x_dbl[:, :rank])
         ctx.is_variable_B = B is None
         ctx.is_variable_C = C is None
         ctx.B_proj_bias_is_None = B_proj_bias is None
@@ -215,15 +221,15 @@ class MambaInnerFn(torch.autograd.Function):
         if B is None:
             B = x_dbl[:, rank:rank + d_state]
             if B_proj_bias is not None:
-                B = B + B_proj_bias.to(B.dtype)
-            B = B.view(xz.shape[0], L, d_state).transpose(1, 2).unsqueeze(1).contiguous()
+                B = B + B_proj_bias.to(B.dtype).unsqueeze(-1)
+            B = B.unsqueeze(1)
         else:
             B = _last_dim_contig(B)
         if C is None:
-            C = x_dbl[:, -d_state:]
+            C = x_dbl[:, rank + d_state:rank + 2 * d_state]
             if C_proj_bias is not None:
-                C = C + C_proj_bias.to(C.dtype)
-            C = C.view(xz.shape[0], L, d_state).transpose(1, 2).unsqueeze(1).contiguous()
+                C = C + C_proj_bias.to(C.dtype).unsqueeze(-1)
+            C = C.unsqueeze(1)
         else:
             C = _last_dim_contig(C)
         if D is not None:
@@ -260,7 +266,7 @@ class MambaInnerFn(torch.autograd.Function):
         dout = _last_dim_contig(dout)
         if ctx.checkpoint_lvl == 1:
             conv_out = causal_conv1d_fwd_function(x, w_conv, conv1d_bias, None, None, None, True)
-            delta = (delta_proj_weight @ x_dbl[:, :rank].t()).view(-1, batch, L).transpose(0, 1)
+            delta = torch.bmm(_bcast(delta_proj_weight, batch), x_dbl[:, :rank])
             # the reference's recompute (selective_scan_interface.py:572-589): delta is normalised
             # again from the projection, and the SAVED (already normalised) B / C are normalised
             # a second time; both are kept so that the gradients equal the reference's
@@ -281,26 +287,21 @@ class MambaInnerFn(torch.autograd.Function):
         out_z_rows = out_z.transpose(0, 1).reshape(out_z.shape[1], -1)  # (d, b*l)
         dout_proj_weight = dout2 @ out_z_rows.t()
         dout_proj_bias = dout.sum(dim=(0, 1)) if not ctx.out_proj_bias_is_None else None
+        # x_dbl is (b, dt_rank + 2n, l): dB / dC are its gradient rows as they come from the scan
         dx_dbl = torch.empty_like(x_dbl)
         dB_proj_bias = dC_proj_bias = None
         if ctx.is_variable_B:
-            dB_rows = dB.squeeze(1).transpose(1, 2).reshape(-1, d_state)
-            dB_proj_bias = dB_rows.sum(0) if not ctx.B_proj_bias_is_None else None
-            dx_dbl[:, rank:rank + d_state] = dB_rows
+            dB_proj_bias = dB.sum(dim=(0, 1, 3)) if not ctx.B_proj_bias_is_None else None
+            dx_dbl[:, rank:rank + d_state] = dB.squeeze(1)
             dB = None
         if ctx.is_variable_C:
-            dC_rows = dC.squeeze(1).transpose(1, 2).reshape(-1, d_state)
-            dC_proj_bias = dC_rows.sum(0) if not ctx.C_proj_bias_is_None else None
-            dx_dbl[:, -d_state:] = dC_rows
+            dC_proj_bias = dC.sum(dim=(0, 1, 3)) if not ctx.C_proj_bias_is_None else None
+            dx_dbl[:, rank + d_state:rank + 2 * d_state] = dC.squeeze(1)
             dC = None
-        ddelta_rows = ddelta.transpose(0, 1).reshape(ddelta.shape[1], -1)  # (d, b*l)
-        ddelta_proj_weight = ddelta_rows @ x_dbl[:, :rank]
-        dx_dbl[:, :rank] = ddelta_rows.t() @ delta_proj_weight
-        conv_rows = conv_out.transpose(1, 2).reshape(-1, conv_out.shape[1])  # (b*l, d)
-        dx_proj_weight = dx_dbl.t() @ conv_rows
-        dconv_rows = dconv_out.transpose(0, 1).reshape(dconv_out.shape[1], -1)  # (d, b*l), a copy
-        dconv_rows = torch.addmm(dconv_rows, x_proj_weight.t(), dx_dbl.t())
-        dconv_out = dconv_rows.view(-1, batch, L).transpose(0, 1)
+        ddelta_proj_weight = torch.bmm(ddelta, x_dbl[:, :rank].transpose(1, 2)).sum(0)
+        torch.bmm(_bcast(delta_proj_weight.t(), batch), ddelta, out=dx_dbl[:, :rank])
+        dx_proj_weight = torch.bmm(dx_dbl, conv_out.transpose(1, 2)).sum(0)
+        dconv_out = torch.baddbmm(dconv_out, _bcast(x_proj_weight.t(), batch), dx_dbl)
         dx, dconv_w, dconv_b, _ = causal_conv1d_bwd_function(x, w_conv, conv1d_bias, dconv_out, None, None, None,
                                                              dx, False, True)
         dconv_b = dconv_b if conv1d_bias is not None else None

@@ -73,7 +73,9 @@ CASES = [
     (1, 16, 1000, 8, torch.float16, 0, True, True, True, True),
     (2, 32, 300, 4, torch.float32, 2, True, True, True, True),
     (1, 4, 2049, 16, torch.bfloat16, 0, True, True, True, True),   # time-split forward
-    (1, 8, 9000, 16, torch.float32, 0, True, True, True, True),    # 113 segments, 4 per carry-scan lane
+    (1, 8, 9000, 16, torch.float32, 0, True, True, True, True),    # 113 segments
+    (1, 8, 1088, 16, torch.float32, 0, True, True, True, True),    # 17 segments: 16 carries, 2 whole batches
+    (1, 8, 1088, 64, torch.float32, 0, True, True, True, True),    # the same, a row's states over 2 warps
     (3, 130, 130, 16, torch.float32, 0, True, True, True, True),   # partial channel tiles
     (1, 8, 70, 1, torch.float32, 0, True, True, True, True),
     (1, 8, 70, 13, torch.float32, 0, True, True, True, True),
