@@ -263,6 +263,8 @@ def main():
     ap.add_argument("--global-batch", type=int, default=None,
                     help="prefill workload: override the global batch (e.g. 2 = one GPU's share at 8 GPUs)")
     ap.add_argument("--no-decode", action="store_true", help="prefill workload: skip the decode measurement")
+    ap.add_argument("--breakdown", action="store_true",
+                    help="prefill workload: add the per-kernel device time of one eager prefill (torch profiler)")
     ap.add_argument("--tp-chunks", type=int, default=1,
                     help="tp workload: sequence chunks whose out_proj all-reduces overlap the next chunk's compute")
     ap.add_argument("--once", action="store_true", help="kernels workload: run each kernel twice (ncu capture)")
@@ -639,6 +641,25 @@ def _cpu_prefill_tok_s(threads, seqlen=512):
                        f"oracle restatement of mamba_inner_ref in fp32: {dt:.2f} s, extrapolated to 24 layers")
 
 
+def _prefill_breakdown(model, ids):
+    """Device time per kernel of one eager (not graphed) prefill, from the torch profiler's CUDA
+    activity records: the same kernels the graph replays, with their launch counts and shares."""
+    from torch.profiler import ProfilerActivity, profile
+    with torch.no_grad():
+        for _ in range(2):
+            model(ids, num_last_tokens=1)
+        torch.cuda.synchronize()
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            model(ids, num_last_tokens=1)
+            torch.cuda.synchronize()
+    ev = [(k.key, k.device_time_total, k.count) for k in prof.key_averages() if k.device_time_total > 0]
+    tot = sum(t for _, t, _ in ev)
+    ev.sort(key=lambda e: -e[1])
+    return {"total_ms": tot / 1e3,
+            "kernels": [{"kernel": k[:120], "launches": c, "us_per_launch": round(t / c, 2),
+                         "total_ms": round(t / 1e3, 4), "share": round(t / tot, 4)} for k, t, c in ev]}
+
+
 def measure_prefill(args, world, rank, local, dev, with_decode=True, with_e2e=True):
     """Config 2: 24-layer MotifMamba stack, bf16 random init, vocab 512 random ids.  Prefill of
     a fixed global batch of 16 x 4096 split over ranks (strong scaling; no collective: each rank
@@ -705,6 +726,9 @@ def measure_prefill(args, world, rank, local, dev, with_decode=True, with_e2e=Tr
         rec["decode_tok_s"] = db * world * P["decode_steps"] / (td.item() * 1e-3)
         rec["decode"] = {"global_batch": db * world, "steps": P["decode_steps"], "prompt": P["prompt"],
                          "cuda_graph": True}
+
+    if getattr(args, "breakdown", False) and rank == 0:
+        rec["kernel_breakdown"] = _prefill_breakdown(model, ids)
 
     if with_e2e:  # end to end: host ids in, last-token logits out
         host_ids = ids.cpu().pin_memory()
