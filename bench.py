@@ -257,6 +257,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="scan workload: skip the config-2 prefill sub-record")
+    ap.add_argument("--no-sweep", action="store_true",
+                    help="scan workload: skip the config-4 sub-records at seqlen 1024 and 16384")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the per-GPU batch (profiling a smaller case of the same kernels)")
     ap.add_argument("--seqlen", type=int, default=None, help="override the sequence length")
@@ -357,6 +359,11 @@ def main():
         e2e = run_e2e(t, dout, dev, stream, world, selective_scan_fn, fwd_b + bwd_b, max(3, args.steps // 4),
                       dist if world > 1 else None)
 
+    # ---- config 4 at the sweep's other sequence lengths (same kernels, same timing) ----
+    sweep = None
+    if not args.no_sweep:
+        sweep = scan_sweep(dev, rank, world, stream, dist if world > 1 else None)
+
     # ---- config-2 prefill (strong scaling over the ranks) and, at world > 1, the TP parity check ----
     prefill = None
     if not args.no_prefill:
@@ -397,6 +404,7 @@ def main():
             "clocks": clocks,
             "e2e": e2e,
             "cpu_baseline": cpu,
+            "seqlen_sweep": sweep,
             "prefill": prefill,
             "tp_check": tpc,
         }
@@ -440,6 +448,56 @@ def tp_check(world, rank, dev, seqlen=1024, n_layer=2, n_chunks=2):
     del model
     torch.cuda.empty_cache()
     dist.barrier()
+    return res
+
+
+def scan_sweep(dev, rank, world, stream, dist, seqlens=(1024, 16384), steps=5, warmup=3):
+    """BASELINE config 4 at its other sequence lengths: batch 32 x 3072 channels per GPU, bf16,
+    fwd + bwd per step as in the headline, CUDA events on the launching stream, max over ranks.
+    Inputs are larger than L2 at every length (0.2 GB per tensor at 1024), so no flush."""
+    from motif_ssm import selective_scan_cuda as ssc
+    saved, res = CFG["seqlen"], {}
+    try:
+        for L in seqlens:
+            CFG["seqlen"] = L
+            t, dout = make_inputs(dev, seed=4321 + rank)
+            fb, bb = algo_bytes(**CFG)
+            evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+
+            def step(ev=None):
+                if ev is not None:
+                    ev[0].record(stream)
+                out, x, _ = ssc.fwd(t["u"], t["delta"], t["A"], t["B"], t["C"], D=t["D"], z=t["z"],
+                                    delta_bias=t["delta_bias"], delta_softplus=True)
+                if ev is not None:
+                    ev[1].record(stream)
+                ssc.bwd(t["u"], t["delta"], t["A"], t["B"], t["C"], D=t["D"], z=t["z"], delta_bias=t["delta_bias"],
+                        dout=dout, x=x, out=out, dz=None, delta_softplus=True, recompute_out_z=False)
+                if ev is not None:
+                    ev[2].record(stream)
+
+            for _ in range(warmup):
+                step()
+            torch.cuda.synchronize()
+            if dist is not None:
+                dist.barrier()
+            for i in range(steps):
+                step(evs[i])
+            torch.cuda.synchronize()
+            tt = torch.tensor([sum(e[0].elapsed_time(e[2]) for e in evs) / steps], device=dev, dtype=torch.float64)
+            if dist is not None:
+                dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+            bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+            peak = hbm_peak()[0]
+            res[str(L)] = {"shape": f"{CFG['batch']} x {CFG['dim']} x {L} per GPU", "steps": steps, "warmup": warmup,
+                           "ms_per_step": tt.item(), "GB/s": (fb + bb) * world / (tt.item() * 1e-3) / 1e9,
+                           "ss_fwd": {"ms": fwd_ms, "frac_of_hbm": fb / (fwd_ms * 1e-3) / 1e9 / peak},
+                           "ss_bwd": {"ms": bwd_ms, "frac_of_hbm": bb / (bwd_ms * 1e-3) / 1e9 / peak}}
+            del t, dout
+            torch.cuda.empty_cache()
+    finally:
+        CFG["seqlen"] = saved
     return res
 
 
