@@ -266,7 +266,7 @@ def main():
                     help="prefill workload: override the global batch (e.g. 2 = one GPU's share at 8 GPUs)")
     ap.add_argument("--no-decode", action="store_true", help="prefill workload: skip the decode measurement")
     ap.add_argument("--breakdown", action="store_true",
-                    help="prefill workload: add the per-kernel device time of one eager prefill (torch profiler)")
+                    help="prefill / tp workloads: add the per-kernel device time of one eager prefill (torch profiler)")
     ap.add_argument("--tp-chunks", type=int, default=1,
                     help="tp workload: sequence chunks whose out_proj all-reduces overlap the next chunk's compute")
     ap.add_argument("--once", action="store_true", help="kernels workload: run each kernel twice (ncu capture)")
@@ -699,21 +699,24 @@ def _cpu_prefill_tok_s(threads, seqlen=512):
                        f"oracle restatement of mamba_inner_ref in fp32: {dt:.2f} s, extrapolated to 24 layers")
 
 
-def _prefill_breakdown(model, ids):
-    """Device time per kernel of one eager (not graphed) prefill, from the torch profiler's CUDA
-    activity records: the same kernels the graph replays, with their launch counts and shares."""
+def _kernel_breakdown(fn):
+    """Device time per kernel of one call of ``fn`` (run eagerly, not graphed), from the torch
+    profiler's CUDA activity records: launch counts, time and share per kernel, and the share of
+    NCCL kernels (whose device time includes waiting for the other ranks).  Every rank must
+    call this together when ``fn`` issues collectives."""
     from torch.profiler import ProfilerActivity, profile
     with torch.no_grad():
         for _ in range(2):
-            model(ids, num_last_tokens=1)
+            fn()
         torch.cuda.synchronize()
         with profile(activities=[ProfilerActivity.CUDA]) as prof:
-            model(ids, num_last_tokens=1)
+            fn()
             torch.cuda.synchronize()
     ev = [(k.key, k.device_time_total, k.count) for k in prof.key_averages() if k.device_time_total > 0]
     tot = sum(t for _, t, _ in ev)
+    nccl = sum(t for k, t, _ in ev if "nccl" in k.lower())
     ev.sort(key=lambda e: -e[1])
-    return {"total_ms": tot / 1e3,
+    return {"total_ms": tot / 1e3, "nccl_ms": nccl / 1e3, "nccl_share": round(nccl / tot, 4) if tot else 0.0,
             "kernels": [{"kernel": k[:120], "launches": c, "us_per_launch": round(t / c, 2),
                          "total_ms": round(t / 1e3, 4), "share": round(t / tot, 4)} for k, t, c in ev]}
 
@@ -786,7 +789,7 @@ def measure_prefill(args, world, rank, local, dev, with_decode=True, with_e2e=Tr
                          "cuda_graph": True}
 
     if getattr(args, "breakdown", False) and rank == 0:
-        rec["kernel_breakdown"] = _prefill_breakdown(model, ids)
+        rec["kernel_breakdown"] = _kernel_breakdown(lambda: model(ids, num_last_tokens=1))
 
     if with_e2e:  # end to end: host ids in, last-token logits out
         host_ids = ids.cpu().pin_memory()
@@ -1018,8 +1021,10 @@ def run_tp(args):
     tt = torch.tensor([s.elapsed_time(e) / args.steps], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    breakdown = _kernel_breakdown(step) if args.breakdown else None  # every rank (collectives)
     if rank == 0:
         print(json.dumps({
+            "kernel_breakdown": breakdown,
             "metric": "MotifMamba TP prefill tok/s (config 3)", "value": L / (tt.item() * 1e-3), "unit": "tok/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": tt.item(),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",

@@ -176,7 +176,7 @@ typedef struct {
  * fused_add_norm and residual_in_fp32, mamba_ssm/models/mixer_seq_simple.py:190-211):
  * residual_out = x + residual_in (residual_in NULL: x), out = residual_out * rsqrt(mean(
  * residual_out^2) + eps) * weight, computed in fp32 from residual_out as stored.  Rows of
- * `dim` elements (dim % 8 == 0, <= 2048) with unit stride and 16-byte-aligned row starts. */
+ * `dim` elements (dim % 8 == 0, <= 4096) with unit stride and 16-byte-aligned row starts. */
 typedef struct {
     int64_t rows, dim;
     int32_t itype;      /* x and out */

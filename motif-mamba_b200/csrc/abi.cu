@@ -438,8 +438,8 @@ int add_rms_norm(const add_rms_norm_args *a, void *stream) {
     for (int t : {a->rin_type, a->rout_type, a->wtype})
         if (t != MSS_F32 && t != a->itype) return fail(MSS_ERR_INVALID, "add_rms_norm: residual / weight type must be f32 or itype");
     if (a->rows < 0 || a->dim < 0) return fail(MSS_ERR_INVALID, "add_rms_norm: negative size");
-    if (a->dim % 8 != 0 || a->dim > 2048)
-        return fail(MSS_ERR_UNSUPPORTED, "add_rms_norm: dim must be a multiple of 8 and at most 2048");
+    if (a->dim % 8 != 0 || a->dim > 4096)
+        return fail(MSS_ERR_UNSUPPORTED, "add_rms_norm: dim must be a multiple of 8 and at most 4096");
     if (a->rows == 0 || a->dim == 0) return MSS_OK;
     if (!a->x || !a->residual_out || !a->weight || !a->out)
         return fail(MSS_ERR_INVALID, "add_rms_norm: x, residual_out, weight and out must be non-null");

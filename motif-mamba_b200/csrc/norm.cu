@@ -14,7 +14,7 @@ namespace mss {
 
 namespace nrm {
 constexpr int NT = 256;      // 8 rows (warps) per CTA
-constexpr int MAXV = 8;      // up to 8 vectors of 8 per lane: rows of up to 2048 elements in registers
+constexpr int MAXV = 16;     // up to 16 vectors of 8 per lane: rows of up to 4096 elements in registers
 }  // namespace nrm
 
 template <typename T, typename RIN, typename ROUT, typename WT, int NV>
@@ -75,7 +75,9 @@ static cudaError_t arn_nv(const add_rms_norm_args &a, cudaStream_t st) {
     if (nv <= 1) add_rms_norm_kernel<T, RIN, ROUT, WT, 1><<<blocks, nrm::NT, 0, st>>>(a);
     else if (nv <= 2) add_rms_norm_kernel<T, RIN, ROUT, WT, 2><<<blocks, nrm::NT, 0, st>>>(a);
     else if (nv <= 4) add_rms_norm_kernel<T, RIN, ROUT, WT, 4><<<blocks, nrm::NT, 0, st>>>(a);
-    else add_rms_norm_kernel<T, RIN, ROUT, WT, 8><<<blocks, nrm::NT, 0, st>>>(a);
+    else if (nv <= 8) add_rms_norm_kernel<T, RIN, ROUT, WT, 8><<<blocks, nrm::NT, 0, st>>>(a);
+    else if (nv <= 12) add_rms_norm_kernel<T, RIN, ROUT, WT, 12><<<blocks, nrm::NT, 0, st>>>(a);
+    else add_rms_norm_kernel<T, RIN, ROUT, WT, 16><<<blocks, nrm::NT, 0, st>>>(a);
     return cudaGetLastError();
 }
 template <typename T, typename RIN, typename ROUT>

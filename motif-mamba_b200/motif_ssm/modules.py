@@ -541,7 +541,8 @@ def tp_prefill(model, input_ids, n_chunks=1, num_last_tokens=1):
     mixer0 = backbone.layers[0].mixer
     world, group = mixer0.world, mixer0.group
     batch, seqlen = input_ids.shape
-    step = max(64, -(-seqlen // n_chunks + 63) // 64 * 64)  # chunk length: a multiple of 64 steps
+    per = -(-seqlen // n_chunks)                 # ceil(seqlen / n_chunks)
+    step = max(64, -(-per // 64) * 64)           # chunk length: rounded up to a multiple of 64 steps
     bounds = [(t, min(seqlen, t + step)) for t in range(0, seqlen, step)]
     emb = backbone.embedding(input_ids)
     hid = [emb[:, t0:t1].contiguous() for t0, t1 in bounds]

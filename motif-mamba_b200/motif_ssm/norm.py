@@ -21,7 +21,7 @@ from .selective_scan_cuda import _itype, _ptr, _stream
 def supported(x, residual, weight):
     """Whether the kernel takes these tensors (else use the torch expression)."""
     D = x.shape[-1]
-    ok = (x.is_cuda and D % 8 == 0 and D <= 2048 and x.stride(-1) == 1 and weight.is_contiguous()
+    ok = (x.is_cuda and D % 8 == 0 and D <= 4096 and x.stride(-1) == 1 and weight.is_contiguous()
           and weight.dtype in (torch.float32, x.dtype) and x.dtype in (torch.float32, torch.float16, torch.bfloat16))
     if residual is not None:
         ok = ok and residual.shape == x.shape and residual.stride(-1) == 1 and residual.dtype in (torch.float32, x.dtype)

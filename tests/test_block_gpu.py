@@ -292,22 +292,27 @@ def test_mamba_inner_rms_options(which, checkpoint_lvl):
                 assert_close(dl[k].grad, leaves[k].grad, 1e-3, 1e-3, f"{which} d{k}", scaled=k != "xz")
 
 
-@pytest.mark.parametrize("dtype,rdtype,with_res", [(torch.bfloat16, torch.float32, True),
-                                                  (torch.bfloat16, torch.float32, False),
-                                                  (torch.float32, torch.float32, True),
-                                                  (torch.float16, torch.float16, True)])
-def test_add_rms_norm_fused(dtype, rdtype, with_res):
+@pytest.mark.parametrize("dtype,rdtype,with_res,D", [(torch.bfloat16, torch.float32, True, 768),
+                                                    (torch.bfloat16, torch.float32, False, 768),
+                                                    (torch.float32, torch.float32, True, 768),
+                                                    (torch.float16, torch.float16, True, 768),
+                                                    (torch.bfloat16, torch.float32, True, 2560),  # config 3
+                                                    (torch.float32, torch.float32, True, 4096),
+                                                    (torch.bfloat16, torch.float32, True, 1544)])
+def test_add_rms_norm_fused(dtype, rdtype, with_res, D):
     """Fused residual add + RMSNorm (the reference stack's fused_add_norm Add -> Norm) against
-    the torch expression in fp32, forward and backward."""
-    from motif_ssm.norm import add_rms_norm
+    the torch expression in fp32, forward and backward, for rows of 768 (config 2), 2560
+    (config 3), 1544 (a partial last vector group) and 4096 (the widest row the kernel takes)."""
+    from motif_ssm.norm import add_rms_norm, supported
     g = torch.Generator().manual_seed(4)
-    rows, D = 300, 768
+    rows = 300
     x = torch.randn(rows, D, generator=g).to(dtype)
     res = torch.randn(rows, D, generator=g).to(rdtype) if with_res else None
     w = (1 + 0.2 * torch.randn(D, generator=g)).to(dtype)
     dy = torch.randn(rows, D, generator=g).to(dtype)
     dr = torch.randn(rows, D, generator=g).to(rdtype)
     leaves = [t.to(DEV).clone().requires_grad_(True) if t is not None else None for t in (x, res, w)]
+    assert supported(leaves[0], leaves[1], leaves[2])  # the fused kernel, not the torch expression
     out, rout = add_rms_norm(leaves[0], leaves[1], leaves[2], 1e-5, rdtype == torch.float32)
     (out.float() * dy.to(DEV).float()).sum().add_((rout.float() * dr.to(DEV).float()).sum()).backward()
     ref_leaves = [t.float().clone().requires_grad_(True) if t is not None else None for t in (x, res, w)]
