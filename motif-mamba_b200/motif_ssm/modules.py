@@ -506,11 +506,81 @@ class TPMambamotif(nn.Module):
                                     self.P_eff, self.Q)
         return y.transpose(1, 2).reshape(-1, self.d_local) @ self.out_proj_w.t()
 
-    @torch.no_grad()
     def forward(self, hidden_states, inference_params=None):
-        batch, seqlen, _ = hidden_states.shape
-        out = self.forward_chunk(hidden_states, {})
-        return self._all_reduce(out.contiguous()).view(batch, seqlen, self.d_model)  # all-reduce #2
+        """Prefill (no autograd): ``forward_chunk`` over the whole sequence and the out_proj
+        all-reduce.  With autograd on (training), ``forward_train``."""
+        if torch.is_grad_enabled() and any(p.requires_grad for p in self.parameters()):
+            return self.forward_train(hidden_states)
+        with torch.no_grad():
+            batch, seqlen, _ = hidden_states.shape
+            out = self.forward_chunk(hidden_states, {})
+            return self._all_reduce(out.contiguous()).view(batch, seqlen, self.d_model)  # all-reduce #2
+
+    def forward_train(self, hidden_states):
+        """The shard's mixer with autograd (the sharded counterpart of the unsharded mixer's
+        training forward).  The replicated input enters through an operator whose backward
+        all-reduces its gradient (each rank's in_proj rows see only this rank's channels); the
+        x_proj and out_proj partial sums leave through an all-reduce whose backward is the
+        identity for out_proj (every rank continues with the same replicated values, so each
+        already holds the full gradient) and an all-reduce for x_proj (each rank uses the full
+        x_dbl for its own channels only).  x_proj partial sums are reduced in fp32 and rounded once, as in the
+        prefill path.  The motif P / Q coupling is not trained here (its sharded copies are
+        not parameters)."""
+        if self.P_eff is not None:
+            raise NotImplementedError("TPMambamotif: training with the motif P/Q coupling is not supported")
+        h = _TPCopy.apply(hidden_states, self.group, self.world)
+        xz = torch.matmul(self.in_proj_w, h.transpose(1, 2))                  # (b, 2 d_local, l)
+        x, z = xz.chunk(2, dim=1)
+        xc = causal_conv1d_fn(x, self.conv_w, self.conv_b, activation="silu")
+        x_dbl = F.linear(xc.transpose(1, 2).float(), self.x_proj_w.float())   # (b, l, r + 2n) partial sums
+        x_dbl = _TPReduce.apply(x_dbl, self.group, self.world, True).to(xc.dtype)  # all-reduce #1
+        dt, B, C = torch.split(x_dbl, [self.dt_rank, self.d_state, self.d_state], dim=-1)
+        delta = torch.matmul(self.dt_proj_w, dt.transpose(1, 2))               # (b, d_local, l)
+        B = B.transpose(1, 2).contiguous()
+        C = C.transpose(1, 2).contiguous()
+        y = selective_scan_fn(xc, delta, -torch.exp(self.A_log), B, C, self.D, z=z, delta_bias=self.dt_proj_b,
+                              delta_softplus=True)
+        out = F.linear(y.transpose(1, 2), self.out_proj_w)                     # (b, l, d_model) partial sums
+        return _TPReduce.apply(out.contiguous(), self.group, self.world, False)  # all-reduce #2
+
+
+class _TPCopy(torch.autograd.Function):
+    """Replicated activations into a channel shard: identity forward, gradient all-reduced."""
+
+    @staticmethod
+    def forward(ctx, x, group, world):
+        ctx.group, ctx.world = group, world
+        return x
+
+    @staticmethod
+    def backward(ctx, g):
+        if ctx.world > 1:
+            g = g.contiguous()
+            torch.distributed.all_reduce(g, group=ctx.group)
+        return g, None, None
+
+
+class _TPReduce(torch.autograd.Function):
+    """Partial sums of the shards summed into full values (all-reduce forward).  Backward: when
+    every rank then uses the full value for its own channels only (x_dbl feeds this rank's
+    dt_proj rows and scan), each rank's gradient is a partial one and is all-reduced
+    (``sharded_after``); when every rank continues with the same replicated computation (the
+    out_proj sum feeds the residual stream), each rank already holds the full gradient."""
+
+    @staticmethod
+    def forward(ctx, x, group, world, sharded_after):
+        ctx.group, ctx.world, ctx.sharded_after = group, world, sharded_after
+        x = x.contiguous().clone()
+        if world > 1:
+            torch.distributed.all_reduce(x, group=group)
+        return x
+
+    @staticmethod
+    def backward(ctx, g):
+        if ctx.sharded_after and ctx.world > 1:
+            g = g.contiguous().clone()
+            torch.distributed.all_reduce(g, group=ctx.group)
+        return g, None, None, None
 
 
 def _scan_chunk(u, delta, A, B, C, D, z, delta_bias, h0, P=None, Q=None):

@@ -119,3 +119,65 @@ def test_tp2_gloo_chunked_prefill_matches_unsharded():
         assert p.exitcode == 0
     for rank, err, scale in res:
         assert err <= 1e-4 * max(1.0, scale), (rank, err, scale)
+
+
+def _grad_worker(rank, world, port, q):
+    """Training through the shards: loss = sum(logits * W) for a fixed W; the sharded
+    parameters' gradients must equal the matching slices of the unsharded model's."""
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [root, os.path.join(root, "motif-mamba_b200")]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        modules = _patch_ops()
+        torch.manual_seed(0)
+        model = modules.MambaLMHeadModel(modules.MambaConfig(d_model=32, n_layer=2, vocab_size=40,
+                                                             ssm_cfg={"d_state": 8}))
+        g = torch.Generator().manual_seed(1)
+        ids = torch.randint(0, 40, (2, 24), generator=g)
+        wl = torch.randn(2, 24, 40, generator=g)
+        ref_logits = model(ids)
+        (ref_logits * wl).sum().backward()
+        full = [(layer.mixer.d_inner, {k: v.grad.clone() for k, v in layer.mixer.named_parameters()})
+                for layer in model.backbone.layers]
+        emb_ref = model.backbone.embedding.weight.grad.clone()
+        model.zero_grad()
+        modules.shard_model_tp(model, rank, world)
+        logits = model(ids)
+        (logits * wl).sum().backward()
+        errs = {"logits": ((logits - ref_logits).abs().max().item(), ref_logits.abs().max().item()),
+                "embedding": ((model.backbone.embedding.weight.grad - emb_ref).abs().max().item(),
+                              emb_ref.abs().max().item())}
+        for i, (layer, (di, gr)) in enumerate(zip(model.backbone.layers, full)):
+            m, dl = layer.mixer, di // world
+            lo, hi = rank * dl, (rank + 1) * dl
+            want = {"in_proj_w": torch.cat([gr["in_proj.weight"][lo:hi], gr["in_proj.weight"][di + lo:di + hi]]),
+                    "conv_w": gr["conv1d.weight"][lo:hi, 0], "conv_b": gr["conv1d.bias"][lo:hi],
+                    "x_proj_w": gr["x_proj.weight"][:, lo:hi], "dt_proj_w": gr["dt_proj.weight"][lo:hi],
+                    "dt_proj_b": gr["dt_proj.bias"][lo:hi], "A_log": gr["A_log"][lo:hi], "D": gr["D"][lo:hi],
+                    "out_proj_w": gr["out_proj.weight"][:, lo:hi]}
+            for k, w in want.items():
+                got = getattr(m, k).grad
+                errs[f"layer{i}.{k}"] = ((got - w.to(got.dtype)).abs().max().item(), w.abs().max().item())
+        q.put((rank, errs))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp2_gloo_backward_matches_unsharded():
+    """Sharded training step (autograd through the shards and both all-reduces) against the
+    unsharded model: logits, every sharded parameter's gradient slice and the replicated
+    embedding's gradient, on 2 gloo ranks."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_grad_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=240) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, errs in res:
+        for k, (err, scale) in errs.items():
+            assert err <= 1e-4 * max(1.0, scale), (rank, k, err, scale)
