@@ -44,13 +44,23 @@ __device__ __forceinline__ float ldw(const void *p, int64_t i) {
     return to_f<W>(reinterpret_cast<const W *>(p)[i]);
 }
 
+// Work item: one row's block of `tblk` steps (a multiple of 256; the whole row unless rows are
+// too few to give every SM enough warps, see conv_dir).
 template <typename T, typename WT, int KW>
-__global__ void __launch_bounds__(256) conv1d_fwd_kernel(const conv1d_args a, int vec) {
+__global__ void __launch_bounds__(256) conv1d_fwd_kernel(const conv1d_args a, int vec, int tblk) {
     const int lane = threadIdx.x & 31;
     const int64_t nrows = a.batch * a.dim;
+    const int nblk = (int)((a.seqlen + tblk - 1) / tblk);
+    const int64_t items = nrows * nblk;
     const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
     const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-    for (int64_t r = warp; r < nrows; r += nwarps) {
+    for (int64_t it = warp; it < items; it += nwarps) {
+        int64_t r = it;
+        int blk = 0;
+        if (nblk > 1) {  // few rows: items < 2^31 (conv_dir)
+            r = (int64_t)((unsigned)it / (unsigned)nblk);
+            blk = (int)(it - r * nblk);
+        }
         const int64_t b = r / a.dim, c = r - b * a.dim;
         float w[KW];
 #pragma unroll
@@ -58,7 +68,8 @@ __global__ void __launch_bounds__(256) conv1d_fwd_kernel(const conv1d_args a, in
         const float bias = a.bias ? ldw<WT>(a.bias, c) : 0.f;
         const T *xr = reinterpret_cast<const T *>(a.x) + b * a.x_bs + c * a.x_ds;
         T *orow = reinterpret_cast<T *>(a.out) + b * a.out_bs + c * a.out_ds;
-        for (int64_t t0 = (int64_t)lane * 8; t0 < a.seqlen; t0 += 256) {
+        const int64_t tend = min(a.seqlen, (int64_t)(blk + 1) * tblk);
+        for (int64_t t0 = (int64_t)blk * tblk + (int64_t)lane * 8; t0 < tend; t0 += 256) {
             float cur[8], prev[8];
             load8_row(xr, t0, a.seqlen, vec, cur);
             load8_row(xr, t0 - 8, a.seqlen, vec, prev);
@@ -241,12 +252,17 @@ template <typename T, typename WT, int KW>
 static cudaError_t conv_dir(const conv1d_args &a, bool vec, bool bwd, cudaStream_t st) {
     const int64_t nrows = a.batch * a.dim;
     const int threads = 256;
-    const int64_t blocks = std::min<int64_t>((nrows * 32 + threads - 1) / threads, 148 * 16);
+    // Forward with fewer rows than ~48 warps per SM (e.g. a 2 x 1536 batch): a warp walking a
+    // whole row keeps one load in flight at a time, so rows are cut into 1024-step items.
+    const int64_t row_blk = (a.seqlen + 255) / 256 * 256;
+    const int tblk = (!bwd && nrows < 148 * 48 && a.seqlen > 1024) ? 1024 : (int)std::min<int64_t>(row_blk, 1 << 30);
+    const int64_t work = nrows * ((a.seqlen + tblk - 1) / tblk);
+    const int64_t blocks = std::min<int64_t>(((bwd ? nrows : work) * 32 + threads - 1) / threads, 148 * 16);
     if (blocks <= 0) return cudaSuccess;
     if (bwd)
         conv1d_bwd_kernel<T, WT, KW><<<(int)blocks, threads, 0, st>>>(a, vec ? 1 : 0);
     else
-        conv1d_fwd_kernel<T, WT, KW><<<(int)blocks, threads, 0, st>>>(a, vec ? 1 : 0);
+        conv1d_fwd_kernel<T, WT, KW><<<(int)blocks, threads, 0, st>>>(a, vec ? 1 : 0, tblk);
     return cudaGetLastError();
 }
 template <typename T, typename WT>

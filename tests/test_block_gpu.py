@@ -26,6 +26,9 @@ DEV = "cuda"
     (1, 5, 1031, 3, torch.float32, torch.float32, False, True),
     (1, 4, 2049, 2, torch.float32, torch.float32, True, False),
     (2, 6, 264, 4, torch.float16, torch.float16, True, True),
+    # rows cut into 1024-step items (few rows, long sequence) and whole rows (many rows)
+    (1, 12, 3000, 4, torch.bfloat16, torch.bfloat16, True, True),
+    (8, 1024, 260, 4, torch.bfloat16, torch.bfloat16, True, True),
 ])
 def test_causal_conv1d_fwd_bwd(batch, dim, seqlen, width, dtype, wdtype, bias, silu):
     from motif_ssm import causal_conv1d_fn
